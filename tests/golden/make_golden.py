@@ -1,0 +1,128 @@
+"""Generate the committed golden fixtures from the reference's OWN golden code.
+
+Run in the build container, where the reference is mounted read-only:
+
+    python tests/golden/make_golden.py /root/reference
+
+It imports, unmodified, the reference's CPU goldens
+  * ascend-kernel/csrc/ops/fa_fp32_stage1/test/fa_fp32_ref.py
+    (gen_inputs, fa_fp64_ref, fa_fp64_ref_tieband)
+  * ascend-kernel/csrc/ops/lse_merge/test/lse_merge_cases.py
+    (make_inputs, fp64_ref, boundary_cases)
+runs them on small seeded cases and writes their inputs/outputs to
+``tests/golden/*.npz``.  The GPU box never reads the reference; the tests read
+only these fixtures.  Case shapes are scaled-down members of the reference's
+own case lists (run_precision_suite.py:19-36, test_lse_flatten_regression.py:31-47,
+lse_merge_cases.py:14-70) so the fixtures stay small.
+"""
+
+import os
+import sys
+import zlib
+
+import numpy as np
+
+
+def stage1_cases():
+    # (name, batch, kv_seqlens, H, KVH, q_len, block_cols_extra, share_blocks, permute)
+    return [
+        ("min_b1_kv128", 1, [128], 8, 2, 1, 0, True, False),
+        ("kv_448_tail", 3, [448] * 3, 8, 2, 1, 0, True, False),
+        ("varlen_3req", 3, [129, 640, 1024], 4, 1, 1, 0, False, False),
+        ("qlen2_b4", 4, [384] * 4, 8, 2, 2, 0, True, False),
+        ("h2_kvh1", 4, [512] * 4, 2, 1, 1, 0, True, False),
+        ("padded_block_cols", 2, [300, 700], 4, 1, 1, 3, False, False),
+        ("flat_T17_g5", 1, [600], 5, 1, 17, 0, True, False),
+        ("flat_T64_g4", 1, [1100], 4, 1, 64, 0, True, False),
+        ("b8_kvh1_g8", 8, [256] * 8, 8, 1, 1, 0, True, False),
+        ("perm_table_varlen", 5, [77, 513, 1, 260, 1030], 4, 1, 1, 1, False, True),
+    ]
+
+
+def make_stage1(ref_dir, out_dir):
+    sys.path.insert(0, os.path.join(ref_dir, "ascend-kernel/csrc/ops/fa_fp32_stage1/test"))
+    import fa_fp32_ref as R  # the reference's own golden module
+
+    for (name, batch, kvs, H, KVH, qlen, extra, share, permute) in stage1_cases():
+        seed = zlib.crc32(name.encode()) % 2**31
+        cols = None if extra == 0 else max((kv + 127) // 128 for kv in kvs) + extra
+        q, k, v, bt, qs, kvarr, T = R.gen_inputs(batch, kvs, H, KVH, 128, seed=seed,
+                                               q_len=qlen, block_cols=cols,
+                                               share_blocks=share)
+        if permute:
+            # random-permutation physical pages; the
+            # reference golden accepts any table (fa_fp32_ref.py:68-79)
+            rng = np.random.default_rng(seed + 1)
+            perm = rng.permutation(k.shape[0]).astype(np.int32)
+            used = bt.copy()
+            for b in range(batch):
+                nb = (kvs[b] + 127) // 128
+                used[b, :nb] = perm[bt[b, :nb]]
+            bt = used
+        q16, k16, v16 = R.to_bf16_bytes(q), R.to_bf16_bytes(k), R.to_bf16_bytes(v)
+        qf, kf, vf = (x.astype(np.float64) for x in (q16, k16, v16))
+        o, lse = R.fa_fp64_ref(qf, kf, vf, bt, qs, kvarr, 128, H, KVH)
+        o_t, lse_t, A = R.fa_fp64_ref_tieband(qf, kf, vf, bt, qs, kvarr, 128, H, KVH)
+        # the tie-band variant recomputes the same O/LSE; store its bound only
+        assert np.array_equal(o_t, o) and np.array_equal(lse_t, lse)
+        np.savez_compressed(
+            os.path.join(out_dir, f"stage1_{name}.npz"),
+            q_bits=q16.view(np.uint16), k_bits=k16.view(np.uint16), v_bits=v16.view(np.uint16),
+            block_table=bt, q_seqlens=qs, kv_seqlens=kvarr,
+            H=H, KVH=KVH, q_len=qlen,
+            o_ref=o, lse_ref=lse, A_tb=A.astype(np.float32))
+        print("stage1", name, "T", T, "blocks", k.shape[0])
+
+
+def make_merge(ref_dir, out_dir):
+    import torch
+    sys.path.insert(0, os.path.join(ref_dir, "ascend-kernel/csrc/ops/lse_merge/test"))
+    import lse_merge_cases as C  # the reference's own case module
+    C.DEV = "cpu"                # the module only uses DEV as a .to() target
+
+    shapes = [("tiny", (7, 4, 16)), ("odd-rows", (13, 4, 128)), ("single-row", (1, 8, 128))]
+    modes = ["A_tier0", "B_fp32out", "Bp_fp32out_pad", "C_hybrid_bf16"]
+    out = {}
+    for cat, (T, H, D) in shapes:
+        for mode in modes:
+            o1_dtype, _, out_code, padded, *_ = C.MODES[mode]
+            seed = zlib.crc32(f"{cat}/{mode}".encode()) % 2**31
+            o1, o2, l1c, l2c, l1, l2 = C.make_inputs(T, H, D, o1_dtype, padded, seed=seed)
+            ref = C.fp64_ref(o1, o2, l1, l2)
+            key = f"{cat}|{mode}"
+            out[key + "|o1"] = (o1.view(torch.int16).numpy().view(np.uint16)
+                                if o1.dtype == torch.bfloat16 else o1.numpy())
+            out[key + "|o2"] = o2.view(torch.int16).numpy().view(np.uint16)
+            out[key + "|l1"] = l1c.numpy()
+            out[key + "|l2"] = l2c.numpy()
+            out[key + "|out_code"] = np.int64(out_code)
+            out[key + "|ref"] = ref.numpy()
+    # boundary mutators on a reduced production-like shape
+    T, H, D = 2, 8, 128
+    for bname, bfn in C.boundary_cases():
+        for mode in ["B_fp32out", "C_hybrid_bf16"]:
+            o1_dtype, _, out_code, padded, *_ = C.MODES[mode]
+            o1, o2, l1c, l2c, l1, l2 = C.make_inputs(T, H, D, o1_dtype, padded,
+                                                     seed=zlib.crc32(bname.encode()) % 2**31)
+            bfn(o1, o2, l1, l2)
+            ref = C.fp64_ref(o1, o2, l1, l2)
+            key = f"boundary-{bname}|{mode}"
+            out[key + "|o1"] = o1.numpy()
+            out[key + "|o2"] = o2.view(torch.int16).numpy().view(np.uint16)
+            out[key + "|l1"] = l1.numpy()
+            out[key + "|l2"] = l2.numpy()
+            out[key + "|out_code"] = np.int64(out_code)
+            out[key + "|ref"] = ref.numpy()
+    np.savez_compressed(os.path.join(out_dir, "lse_merge_cases.npz"), **out)
+    print("lse_merge", len(out) // 6, "cases")
+
+
+def main():
+    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    out_dir = os.path.dirname(os.path.abspath(__file__))
+    make_stage1(ref_dir, out_dir)
+    make_merge(ref_dir, out_dir)
+
+
+if __name__ == "__main__":
+    main()
