@@ -1,0 +1,165 @@
+/*
+ * cascade_b200.h -- C ABI of the B200 (sm_100a) cascade-decode operator set.
+ *
+ * Plain pointers and sizes only: no torch, no C++ types. Every entry point
+ * runs asynchronously on the given CUDA stream and returns 0 on success or a
+ * cascade_status code; cascade_last_error() gives the message of the last
+ * failure on the calling thread (messages start with the reference op name,
+ * e.g. "fa_fp32_stage1: ...", matching the reference's TORCH_CHECK texts).
+ *
+ * Device pointers are CUDA device (or managed) memory on the current device.
+ * `stream` is a cudaStream_t (0 = legacy default stream).
+ */
+#ifndef CASCADE_B200_H
+#define CASCADE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CASCADE_API __attribute__((visibility("default")))
+#else
+#define CASCADE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *cascade_stream_t; /* == cudaStream_t */
+
+enum cascade_dtype {
+  CASCADE_BF16 = 0,
+  CASCADE_FP16 = 1,
+  CASCADE_FP32 = 2,
+};
+
+enum cascade_status {
+  CASCADE_OK = 0,
+  CASCADE_ERR_INVALID = 1,     /* argument rejected by validation */
+  CASCADE_ERR_CUDA = 2,        /* a CUDA runtime / driver call failed */
+  CASCADE_ERR_WORKSPACE = 3,   /* workspace missing or too small */
+  CASCADE_ERR_UNSUPPORTED = 4, /* shape outside the supported domain */
+};
+
+/* Paged-attention problem description shared by stage-1 and the suffix.
+ * Layouts follow the reference op (ascend-kernel/csrc/ops.h:26-38,
+ * ascend-kernel/README.md:122-131):
+ *   query        [num_tokens, num_heads, head_dim], contiguous
+ *   key / value  [num_blocks, block_size, kv_heads, head_dim], contiguous
+ *   block_table  int32 [batch, block_cols]; block_cols is the row stride
+ *   actual_q_seqlens / actual_kv_seqlens  int64 [batch], DEVICE memory
+ * q_seqlen_value > 0: every request has that many query tokens (no device->
+ * host reads; graph-capture safe). q_seqlen_value == 0: the seqlens are read
+ * back to the host and validated (the reference's legacy path,
+ * ascend-kernel/csrc/ops/fa_fp32_stage1/op_host/fa_fp32_stage1.cpp:215-246).
+ */
+typedef struct cascade_paged_attn {
+  const void *query;
+  const void *key;
+  const void *value;
+  const int32_t *block_table;
+  const int64_t *actual_q_seqlens;
+  const int64_t *actual_kv_seqlens;
+  int64_t num_tokens;
+  int64_t num_heads;
+  int64_t head_dim;
+  int64_t num_blocks;
+  int64_t block_size;
+  int64_t kv_heads;
+  int64_t batch;
+  int64_t block_cols;
+  int64_t q_seqlen_value;
+  int32_t dtype; /* cascade_dtype of query/key/value: BF16 or FP16 */
+  int32_t flags; /* reserved, pass 0 */
+} cascade_paged_attn_t;
+
+/* Bytes of device workspace a call with this description needs (split-KV
+ * partials). Depends on shapes only, never on the seqlen values. 0 = none. */
+CASCADE_API size_t cascade_fa_fp32_stage1_workspace_size(const cascade_paged_attn_t *p);
+
+/* Stage-1 shared-prefix paged attention, fp32 out + padded LSE.
+ * Replaces ascend_kernel::fa_fp32_stage1
+ *   (ascend-kernel/csrc/ops/fa_fp32_stage1/op_host/fa_fp32_stage1.cpp:178-329,
+ *    schema ascend-kernel/csrc/register.cpp:25-26).
+ * out: fp32 [num_tokens, num_heads, head_dim]
+ * lse: fp32 [num_tokens * num_heads * 8]; row (token*H + head) holds 8 copies
+ *      of ln(sum exp) + max (the reference's 32-byte padded LSE rows).
+ * A request with kv length 0 (accepted only when q_seqlen_value > 0) yields
+ * out = 0 and lse = -inf. */
+CASCADE_API int cascade_fa_fp32_stage1(const cascade_paged_attn_t *p, float *out, float *lse, void *workspace,
+                           size_t workspace_bytes, cascade_stream_t stream);
+
+/* Stage-2 per-request suffix decode: same problem description, output in the
+ * query dtype and a compact fp32 LSE. Replaces the closed CANN
+ * npu_fused_infer_attention_score_v2 call of the cascade consumer
+ * (ascend-kernel/README.md:180-199; (o2, l2) = (bf16 [B,H,1,D], fp32 [B,H,1])).
+ * out: [num_tokens, num_heads, head_dim] in p->dtype; lse: fp32 [num_tokens*num_heads].
+ * kv length 0 is allowed in both q_seqlen modes: out = 0, lse = -inf. */
+CASCADE_API size_t cascade_suffix_decode_workspace_size(const cascade_paged_attn_t *p);
+CASCADE_API int cascade_suffix_decode(const cascade_paged_attn_t *p, void *out, float *lse, void *workspace,
+                          size_t workspace_bytes, cascade_stream_t stream);
+
+/* Row-wise LSE-space merge of two attention partials.
+ * Replaces ascend_kernel::lse_merge
+ *   (ascend-kernel/csrc/ops/lse_merge/op_host/lse_merge.cpp:32-70,
+ *    schema ascend-kernel/csrc/register.cpp:24).
+ * o1: [rows, dim] BF16 / FP16 / FP32; o2: [rows, dim] BF16 / FP16 / FP32;
+ * lse1/lse2: fp32 with row strides stride1/stride2 (value = element 0 of the row);
+ * out: [rows, dim] in out_dtype. m = max(l1,l2); w = exp(l-m);
+ * out = (o1 w1 + o2 w2) / (w1 + w2) in fp32; a side whose lse is -inf gets
+ * weight 0 (both -inf -> 0). */
+CASCADE_API int cascade_lse_merge(const void *o1, int32_t o1_dtype, const void *o2, int32_t o2_dtype, const float *lse1,
+                      int64_t stride1, const float *lse2, int64_t stride2, void *out, int32_t out_dtype,
+                      int64_t rows, int64_t dim, cascade_stream_t stream);
+
+/* Gate/up GEMM with the f3 epilogue modes.
+ * Replaces ascend_kernel::f3_gateup_epilogue
+ *   (ascend-kernel/csrc/ops/f3_floor/op_host/f3_floor.cpp:59-125,
+ *    schema ascend-kernel/csrc/register.cpp:30-31).
+ * a: bf16 [M, K] (row stride K); b: bf16 [2I, K] (gate rows [0,I), up rows [I,2I));
+ * ws: bf16 [M, 2I] C workspace (may be NULL for mode 1); d: bf16 [M, I] with row stride d_stride.
+ * mode 1: d = silu(a b_gate^T) * (a b_up^T), fp32 epilogue, RNE to bf16, ws untouched.
+ * mode 2: ws = a b^T (bf16), d untouched.
+ * mode 0: ws = a b^T and d = gate half of ws; mode 4: ws = a b^T and d = up half.
+ * mode 3: d = gate half of the existing ws (no GEMM); mode 5: same, gate half only read;
+ * mode 7: read gate+up halves of ws, write nothing; mode 8: write d (zeros), read nothing. */
+CASCADE_API int cascade_f3_gateup_epilogue(const void *a, const void *b, void *ws, void *d, int64_t d_stride, int64_t M,
+                               int64_t K, int64_t I, int32_t mode, cascade_stream_t stream);
+
+/* Last error message of this thread ("" if none). */
+CASCADE_API const char *cascade_last_error(void);
+
+/* Reads and clears the device error word (non-zero = a kernel's bounded
+ * wait gave up). Synchronises the current device. */
+CASCADE_API int cascade_device_error(uint32_t *word);
+
+/* Library version (major*10000 + minor*100 + patch). */
+CASCADE_API int cascade_version(void);
+
+/* Host-only planner used by the entry points (exposed for tests and callers
+ * that size grids): which kernel serves a paged-attention call and how it is
+ * split. No CUDA calls. Returns 0 or CASCADE_ERR_*; the fields are:
+ *   kernel: 0 = decode path (<= 16 query rows per request and kv head),
+ *           1 = tcgen05 tile path (more rows);
+ *   rows_per_group: max query rows per (request, kv head) = q_len * H/KVH;
+ *   split_tokens: kv tokens per split (a multiple of the kernel's KV tile);
+ *   num_splits: splits per request; workspace_bytes: as the *_workspace_size
+ *   functions report. max_q_seqlen: the host-known maximum q length
+ *   (== q_seqlen_value on the uniform path). */
+typedef struct cascade_attn_plan {
+  int32_t kernel;
+  int32_t rows_per_group;
+  int64_t split_tokens;
+  int64_t num_splits;
+  size_t workspace_bytes;
+} cascade_attn_plan_t;
+
+CASCADE_API int cascade_plan_paged_attn(const cascade_paged_attn_t *p, int64_t max_q_seqlen, int32_t suffix_mode,
+                            cascade_attn_plan_t *plan);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CASCADE_B200_H */

@@ -74,6 +74,15 @@ def quantize(x, dtype):
     raise ValueError(dtype)
 
 
+def ulp(x, dtype):
+    """Spacing of the ``dtype`` grid at |x| (bf16: 8 significant bits,
+    fp16: 11, fp32: 24), floored at the smallest normal spacing."""
+    mant = {"bf16": 8, "fp16": 11, "fp32": 24}[dtype]
+    emin = {"bf16": -126, "fp16": -14, "fp32": -126}[dtype]
+    ax = np.maximum(np.abs(np.asarray(x, dtype=np.float64)), 2.0 ** emin)
+    return 2.0 ** (np.floor(np.log2(ax)) - (mant - 1))
+
+
 def bf16_bits(x):
     """fp32 array -> uint16 bf16 bit patterns (RNE)."""
     x32 = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
@@ -126,14 +135,40 @@ def gather_pages(pool, bt_row, kv):
     return rows[:kv]
 
 
-def _segments(kv, split):
+def _contiguous_segments(kv, split, chunk):
+    """[(segment = list of chunk index arrays)] for contiguous splits."""
     if split is None or split <= 0 or split >= kv:
-        return [(0, kv)]
-    return [(s, min(kv, s + split)) for s in range(0, kv, split)]
+        bounds = [(0, kv)]
+    else:
+        bounds = [(s, min(kv, s + split)) for s in range(0, kv, split)]
+    return [[np.arange(c0, min(s1, c0 + chunk)) for c0 in range(s0, s1, chunk)]
+            for (s0, s1) in bounds]
+
+
+def decode_segments(kv, split=256, tile=64, warps=4):
+    """Token structure of the decode kernel (csrc/paged_decode.cu): a CTA owns
+    ``split`` kv tokens, streamed in ``tile``-token stages; warp w of the CTA
+    takes the w-th ``tile/warps`` tokens of every stage and runs its own online
+    softmax over them one stage at a time.  Returns segments as lists of chunk
+    index arrays (empty segments dropped)."""
+    sub = tile // warps
+    segs = []
+    for s0 in range(0, kv, split):
+        s1 = min(kv, s0 + split)
+        for w in range(warps):
+            chunks = []
+            for t0 in range(s0, s1, tile):
+                a = t0 + w * sub
+                b = min(s1, a + sub)
+                if a < b:
+                    chunks.append(np.arange(a, b))
+            if chunks:
+                segs.append(chunks)
+    return segs
 
 
 def paged_attention_ref(q, k, v, block_table, q_seqlens, kv_seqlens, *,
-                        chunk=512, split=None, p_dtype="bf16", scale=None,
+                        chunk=512, split=None, segments=None, p_dtype="bf16", scale=None,
                         with_tieband=False, tie_band_rel=2e-5):
     """fp64 paged attention with the reference kernel's quantisation points.
 
@@ -147,7 +182,9 @@ def paged_attention_ref(q, k, v, block_table, q_seqlens, kv_seqlens, *,
     ``split`` (tokens) partitions each request's kv into independent segments
     whose online softmax starts afresh; the segments are merged exactly in LSE
     space -- the structure of a split-KV kernel.  ``split=None`` is the
-    reference's single pass.
+    reference's single pass.  ``segments`` (a function kv -> list of segments,
+    each an ordered list of chunk index arrays, e.g. ``decode_segments``)
+    overrides chunk/split with an arbitrary token-to-segment assignment.
 
     q: [T,H,D]; k,v: [numBlocks, bs, KVH, D] (values already on the input grid).
     Returns (O [T,H,D] f64, LSE [T,H] f64[, A [T,H,D] tie-band bound]).
@@ -178,16 +215,16 @@ def paged_attention_ref(q, k, v, block_table, q_seqlens, kv_seqlens, *,
         qb = q64[tok:tok + ql].transpose(1, 0, 2)                   # [H,ql,D]
         S = np.einsum("htd,khd->htk", qb, kb) * scale
         seg_o, seg_l, seg_a = [], [], []
-        for (s0, s1) in _segments(kv, split):
+        segs = segments(kv) if segments is not None else _contiguous_segments(kv, split, chunk)
+        for seg in segs:
             m = np.full((H, ql), -np.inf)
             gl = np.zeros((H, ql))
             acc = np.zeros((H, ql, D))
             amb = np.zeros((H, ql, D)) if with_tieband else None
-            for c0 in range(s0, s1, chunk):
-                c1 = min(s1, c0 + chunk)
-                sc = S[:, :, c0:c1]
+            for ci, idx in enumerate(seg):
+                sc = S[:, :, idx]
                 m_new = np.maximum(m, sc.max(axis=2))
-                dm = np.where(c0 == s0, 1.0, np.exp(m - m_new))
+                dm = np.where(ci == 0, 1.0, np.exp(m - m_new))
                 ls = np.exp(sc - m_new[:, :, None])
                 if with_tieband:
                     p, g_lo, g_hi = _neighbours(ls, p_dtype)
@@ -196,11 +233,11 @@ def paged_attention_ref(q, k, v, block_table, q_seqlens, kv_seqlens, *,
                     # accumulated exactly as fa_fp32_ref.py:199-200 does it
                     # (the step's dm scales the new term, not the old bound)
                     amb = amb + dm[:, :, None] * np.einsum(
-                        "htk,khd->htd", ambiguous * (g_hi - g_lo), np.abs(vb[c0:c1]))
+                        "htk,khd->htd", ambiguous * (g_hi - g_lo), np.abs(vb[idx]))
                 else:
                     p = quantize(ls, p_dtype)
                 gl = dm * gl + ls.sum(axis=2)
-                acc = dm[:, :, None] * acc + np.einsum("htk,khd->htd", p, vb[c0:c1])
+                acc = dm[:, :, None] * acc + np.einsum("htk,khd->htd", p, vb[idx])
                 m = m_new
             seg_o.append(acc / gl[:, :, None])
             seg_l.append(np.log(gl) + m)

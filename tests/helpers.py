@@ -1,0 +1,98 @@
+"""Shared helpers for the GPU parity tests (device tensors <-> oracle arrays,
+C-ABI call wrappers)."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import cascade_oracle as O
+
+
+def need_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def capi():
+    from cascade_kernel import capi as C
+    C.load()
+    return C
+
+
+def ops():
+    import cascade_kernel  # noqa: F401  registers torch.ops.npu.*
+    import torch
+    return torch.ops.npu
+
+
+def bits_to_dev(bits, dtype="bf16"):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16))
+    return t.view(torch.bfloat16 if dtype == "bf16" else torch.float16).cuda()
+
+
+def dev_to_f64(t):
+    import torch
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def load_fixture(name):
+    z = np.load(os.path.join(GOLDEN, f"stage1_{name}.npz"))
+    return z
+
+
+def fixture_device_args(z):
+    import torch
+    q = bits_to_dev(z["q_bits"])
+    k = bits_to_dev(z["k_bits"])
+    v = bits_to_dev(z["v_bits"])
+    bt = torch.from_numpy(z["block_table"]).cuda()
+    qs = torch.from_numpy(z["q_seqlens"]).cuda()
+    kvs = torch.from_numpy(z["kv_seqlens"]).cuda()
+    return q, k, v, bt, qs, kvs
+
+
+def fixture_host_args(z):
+    return (O.bf16_bits_to_f64(z["q_bits"]), O.bf16_bits_to_f64(z["k_bits"]),
+            O.bf16_bits_to_f64(z["v_bits"]), z["block_table"], z["q_seqlens"], z["kv_seqlens"])
+
+
+def run_capi_paged(q, k, v, bt, qs, kvs, q_seqlen_value, suffix=False):
+    """Call cascade_fa_fp32_stage1 / cascade_suffix_decode through the C ABI."""
+    import torch
+    C = capi()
+    desc = C.paged_desc(q, k, v, bt, qs, kvs, q_seqlen_value)
+    T, H, D = q.shape
+    if suffix:
+        out = torch.empty((T, H, D), dtype=q.dtype, device=q.device)
+        lse = torch.empty((T * H,), dtype=torch.float32, device=q.device)
+        n = C.suffix_workspace_size(desc)
+    else:
+        out = torch.empty((T, H, D), dtype=torch.float32, device=q.device)
+        lse = torch.empty((T * H * 8,), dtype=torch.float32, device=q.device)
+        n = C.stage1_workspace_size(desc)
+    ws = torch.empty((max(n, 1),), dtype=torch.uint8, device=q.device) if n else None
+    if suffix:
+        C.suffix_decode(desc, out, lse, ws)
+    else:
+        C.fa_fp32_stage1(desc, out, lse, ws)
+    torch.cuda.synchronize()
+    assert C.device_error() == 0
+    return out, lse
+
+
+def kernel_structure(q_len, group, kv_cap_tokens, T, H, KVH, batch, block_cols, block_size, suffix=False):
+    """(kernel id, oracle kwargs reproducing that kernel's quantisation structure)."""
+    C = capi()
+    desc = C.paged_desc(None, None, None, None, None, None, q_len,
+                        shape=dict(num_tokens=T, num_heads=H, head_dim=128, num_blocks=1,
+                                   block_size=block_size, kv_heads=KVH, batch=batch,
+                                   block_cols=block_cols))
+    desc.q_seqlen_value = 0
+    p = C.plan(desc, q_len, suffix)
+    if p.kernel == 0:
+        split = int(p.split_tokens)
+        return 0, dict(segments=lambda kv: O.decode_segments(kv, split=split, tile=64, warps=4))
+    return 1, dict(chunk=128, split=int(p.split_tokens))

@@ -1,0 +1,196 @@
+"""ctypes binding of the C ABI (include/cascade_b200.h).
+
+This is the binding a non-torch host (or a test) uses: plain pointers and
+sizes. ``load()`` opens ``libcascade_b200.so`` without importing the torch
+extension. Tensor helpers accept torch tensors only to read ``data_ptr()``.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libcascade_b200.so")
+
+BF16, FP16, FP32 = 0, 1, 2
+OK, ERR_INVALID, ERR_CUDA, ERR_WORKSPACE, ERR_UNSUPPORTED = 0, 1, 2, 3, 4
+
+EXPORTED = [
+    "cascade_fa_fp32_stage1_workspace_size",
+    "cascade_fa_fp32_stage1",
+    "cascade_suffix_decode_workspace_size",
+    "cascade_suffix_decode",
+    "cascade_lse_merge",
+    "cascade_f3_gateup_epilogue",
+    "cascade_last_error",
+    "cascade_device_error",
+    "cascade_version",
+    "cascade_plan_paged_attn",
+]
+
+
+class PagedAttn(ctypes.Structure):
+    _fields_ = [
+        ("query", ctypes.c_void_p),
+        ("key", ctypes.c_void_p),
+        ("value", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("actual_q_seqlens", ctypes.c_void_p),
+        ("actual_kv_seqlens", ctypes.c_void_p),
+        ("num_tokens", ctypes.c_int64),
+        ("num_heads", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64),
+        ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int64),
+        ("kv_heads", ctypes.c_int64),
+        ("batch", ctypes.c_int64),
+        ("block_cols", ctypes.c_int64),
+        ("q_seqlen_value", ctypes.c_int64),
+        ("dtype", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+    ]
+
+
+class AttnPlan(ctypes.Structure):
+    _fields_ = [
+        ("kernel", ctypes.c_int32),
+        ("rows_per_group", ctypes.c_int32),
+        ("split_tokens", ctypes.c_int64),
+        ("num_splits", ctypes.c_int64),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_lib = None
+
+
+def load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise OSError(f"{LIB_PATH} not built; run vllm-hust-cascade-kernel_b200/build.py")
+    lib = ctypes.CDLL(LIB_PATH)
+    P = ctypes.POINTER(PagedAttn)
+    vp, i64, i32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_size_t
+    lib.cascade_fa_fp32_stage1_workspace_size.argtypes = [P]
+    lib.cascade_fa_fp32_stage1_workspace_size.restype = sz
+    lib.cascade_suffix_decode_workspace_size.argtypes = [P]
+    lib.cascade_suffix_decode_workspace_size.restype = sz
+    lib.cascade_fa_fp32_stage1.argtypes = [P, vp, vp, vp, sz, vp]
+    lib.cascade_fa_fp32_stage1.restype = ctypes.c_int
+    lib.cascade_suffix_decode.argtypes = [P, vp, vp, vp, sz, vp]
+    lib.cascade_suffix_decode.restype = ctypes.c_int
+    lib.cascade_lse_merge.argtypes = [vp, i32, vp, i32, vp, i64, vp, i64, vp, i32, i64, i64, vp]
+    lib.cascade_lse_merge.restype = ctypes.c_int
+    lib.cascade_f3_gateup_epilogue.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
+    lib.cascade_f3_gateup_epilogue.restype = ctypes.c_int
+    lib.cascade_last_error.argtypes = []
+    lib.cascade_last_error.restype = ctypes.c_char_p
+    lib.cascade_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
+    lib.cascade_device_error.restype = ctypes.c_int
+    lib.cascade_version.argtypes = []
+    lib.cascade_version.restype = ctypes.c_int
+    lib.cascade_plan_paged_attn.argtypes = [P, i64, i32, ctypes.POINTER(AttnPlan)]
+    lib.cascade_plan_paged_attn.restype = ctypes.c_int
+    _lib = lib
+    return lib
+
+
+class CascadeError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(msg)
+        self.code = code
+
+
+def check(rc):
+    if rc != OK:
+        raise CascadeError(rc, load().cascade_last_error().decode())
+    return rc
+
+
+def last_error():
+    return load().cascade_last_error().decode()
+
+
+def device_error():
+    w = ctypes.c_uint32(0)
+    check(load().cascade_device_error(ctypes.byref(w)))
+    return w.value
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def dtype_code(torch_dtype):
+    import torch
+    return {torch.bfloat16: BF16, torch.float16: FP16, torch.float32: FP32}[torch_dtype]
+
+
+def paged_desc(query, key, value, block_table, q_seqlens, kv_seqlens, q_seqlen_value=0, *,
+               shape=None, dtype=None):
+    """Build the C descriptor from device tensors (or from explicit shapes when
+    ``shape`` = dict of sizes is given and the tensors are None)."""
+    d = PagedAttn()
+    if shape is None:
+        d.query, d.key, d.value = query.data_ptr(), key.data_ptr(), value.data_ptr()
+        d.block_table = block_table.data_ptr()
+        d.actual_q_seqlens, d.actual_kv_seqlens = q_seqlens.data_ptr(), kv_seqlens.data_ptr()
+        d.num_tokens, d.num_heads, d.head_dim = query.shape
+        d.num_blocks, d.block_size, d.kv_heads = key.shape[0], key.shape[1], key.shape[2]
+        d.batch = q_seqlens.numel()
+        d.block_cols = block_table.shape[1]
+        d.dtype = dtype_code(query.dtype)
+    else:
+        for k, v in shape.items():
+            setattr(d, k, v)
+        d.dtype = BF16 if dtype is None else dtype
+    d.q_seqlen_value = q_seqlen_value
+    d.flags = 0
+    return d
+
+
+def plan(desc, max_q, suffix=False):
+    p = AttnPlan()
+    check(load().cascade_plan_paged_attn(ctypes.byref(desc), max_q, int(suffix), ctypes.byref(p)))
+    return p
+
+
+def stream_ptr(stream=None):
+    import torch
+    s = torch.cuda.current_stream() if stream is None else stream
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def fa_fp32_stage1(desc, out, lse, workspace=None, stream=None):
+    """Call cascade_fa_fp32_stage1 through the C ABI (out/lse/workspace are
+    preallocated device tensors)."""
+    lib = load()
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    return check(lib.cascade_fa_fp32_stage1(ctypes.byref(desc), _ptr(out), _ptr(lse), _ptr(workspace),
+                                            ws_bytes, stream_ptr(stream)))
+
+
+def suffix_decode(desc, out, lse, workspace=None, stream=None):
+    lib = load()
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    return check(lib.cascade_suffix_decode(ctypes.byref(desc), _ptr(out), _ptr(lse), _ptr(workspace),
+                                           ws_bytes, stream_ptr(stream)))
+
+
+def stage1_workspace_size(desc):
+    return load().cascade_fa_fp32_stage1_workspace_size(ctypes.byref(desc))
+
+
+def suffix_workspace_size(desc):
+    return load().cascade_suffix_decode_workspace_size(ctypes.byref(desc))
+
+
+def lse_merge(o1, o2, lse1, stride1, lse2, stride2, out, rows, dim, stream=None):
+    return check(load().cascade_lse_merge(
+        _ptr(o1), dtype_code(o1.dtype), _ptr(o2), dtype_code(o2.dtype), _ptr(lse1), stride1,
+        _ptr(lse2), stride2, _ptr(out), dtype_code(out.dtype), rows, dim, stream_ptr(stream)))
+
+
+def gateup(a, b, ws, d, d_stride, M, K, I, mode, stream=None):
+    return check(load().cascade_f3_gateup_epilogue(
+        _ptr(a), _ptr(b), _ptr(ws), _ptr(d), d_stride, M, K, I, mode, stream_ptr(stream)))

@@ -1,0 +1,58 @@
+"""The two-stage cascade decode step, composed from the registered ops.
+
+Mirrors how the reference's consumer drives the ops (ascend-kernel/README.md:
+158-201): stage-1 reads each shared prefix ONCE for all requests of its prefix
+group (the group's requests are flattened into one "request" whose q_len is
+the group size), stage-2 reads each request's own suffix pages, and the LSE
+merge combines the two partials.
+
+Queries must be ordered by prefix group: group g owns query rows
+``[sum(group_sizes[:g]), sum(group_sizes[:g+1]))``.
+"""
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass
+class CascadeTables:
+    """Per-step index tensors (all on the device).
+
+    prefix_block_table  int32 [G, cols_p]   pages of each group's shared prefix
+    prefix_q_seqlens    int64 [G]           requests per group
+    prefix_kv_seqlens   int64 [G]           prefix length of each group
+    suffix_block_table  int32 [B, cols_s]   pages of each request's own suffix
+    suffix_q_seqlens    int64 [B]           ones
+    suffix_kv_seqlens   int64 [B]           suffix length of each request (may be 0)
+    uniform_group       int                 group size if all groups are equal, else 0
+    """
+    prefix_block_table: torch.Tensor
+    prefix_q_seqlens: torch.Tensor
+    prefix_kv_seqlens: torch.Tensor
+    suffix_block_table: torch.Tensor
+    suffix_q_seqlens: torch.Tensor
+    suffix_kv_seqlens: torch.Tensor
+    uniform_group: int = 0
+
+
+def cascade_decode(q, k_pool, v_pool, tables: CascadeTables, out_dtype=None):
+    """One cascade decode step for one layer.
+
+    q [B, H, 128] (bf16 or fp16), k_pool/v_pool [numBlocks, bs, KVH, 128].
+    Returns the merged attention output [B, H, 128] in ``out_dtype``
+    (default: the query dtype).  bf16 + block size 128 uses exactly the
+    reference ops (fa_fp32_stage1 / lse_merge out_code=1); other inputs use
+    the extended-domain siblings."""
+    out_dtype = q.dtype if out_dtype is None else out_dtype
+    reference_domain = (q.dtype == torch.bfloat16 and k_pool.shape[1] == 128
+                        and out_dtype == torch.bfloat16)
+    npu = torch.ops.npu
+    prefix = npu.fa_fp32_stage1 if reference_domain else npu.cascade_prefix_attention
+    o1, l1 = prefix(q, k_pool, v_pool, tables.prefix_block_table, tables.prefix_q_seqlens,
+                    tables.prefix_kv_seqlens, tables.uniform_group)
+    o2, l2 = npu.cascade_suffix_decode(q, k_pool, v_pool, tables.suffix_block_table,
+                                       tables.suffix_q_seqlens, tables.suffix_kv_seqlens, 1)
+    code = {torch.bfloat16: 1, torch.float32: 2, torch.float16: 3}[out_dtype]
+    if reference_domain:
+        return npu.lse_merge(o1, o2, l1, l2, code)
+    return npu.cascade_lse_merge(o1, o2, l1, l2, code)

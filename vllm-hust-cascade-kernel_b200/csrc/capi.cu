@@ -1,0 +1,380 @@
+// C ABI of the cascade-decode operator set (include/cascade_b200.h):
+// validation (mirroring the reference op hosts' checks and messages),
+// planning (kernel choice and KV splits, shape-only so workspaces can be
+// sized without reading device memory), tensor-map encoding and launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/cascade_b200.h"
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace cascade {
+
+__device__ unsigned int g_cascade_device_error = 0;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(const char* op, cudaError_t e) {
+  return fail(CASCADE_ERR_CUDA, "%s: CUDA error %d (%s)", op, static_cast<int>(e), cudaGetErrorString(e));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  });
+  return fn;
+}
+
+bool block_size_ok(int64_t bs) {
+  return bs == 16 || bs == 32 || bs == 64 || bs == 128 || bs == 256 || bs == 512;
+}
+
+constexpr int kDecodeSplit = 256;  // kv tokens per decode split (multiple of its 64-token tile)
+constexpr int kTcTile = 128;       // kv tokens per tcgen05 tile
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Shape-only split rule of each kernel.
+void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens, int64_t* num_splits) {
+  const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
+  if (kernel == 0) {
+    *split_tokens = kDecodeSplit;
+  } else {
+    const int64_t group = p->num_heads / p->kv_heads;
+    const int64_t mtiles = std::max<int64_t>(p->batch, ceil_div(p->num_tokens * group, 128));
+    const int64_t units = p->kv_heads * mtiles;
+    const int64_t want = ceil_div(2 * kNumSMs, units);
+    int64_t ns = std::min<int64_t>(std::max<int64_t>(want, 1), ceil_div(cap, kTcTile));
+    *split_tokens = ceil_div(ceil_div(cap, ns), kTcTile) * kTcTile;
+  }
+  *num_splits = ceil_div(cap, *split_tokens);
+}
+
+size_t workspace_for(const cascade_paged_attn_t* p, int64_t num_splits) {
+  if (num_splits <= 1) return 0;
+  const size_t rows = static_cast<size_t>(p->num_tokens) * p->num_heads;
+  return static_cast<size_t>(num_splits) * rows * (kHeadDim + 1) * sizeof(float);
+}
+
+// Validation common to both paged-attention entry points; `op` prefixes messages.
+int validate_paged(const cascade_paged_attn_t* p, const char* op) {
+  if (p == nullptr) return fail(CASCADE_ERR_INVALID, "%s: null argument", op);
+  if (p->dtype != CASCADE_BF16 && p->dtype != CASCADE_FP16)
+    return fail(CASCADE_ERR_INVALID, "%s: query/key/value must be bf16 or fp16", op);
+  if (p->q_seqlen_value < 0)
+    return fail(CASCADE_ERR_INVALID, "%s: q_seqlen_value must be >= 0 (0 = read seqlens from device)", op);
+  if (p->head_dim != kHeadDim)
+    return fail(CASCADE_ERR_UNSUPPORTED, "%s: only head dim 128 is supported (L1TileShape::K constraint)", op);
+  if (!block_size_ok(p->block_size))
+    return fail(CASCADE_ERR_UNSUPPORTED, "%s: paged blockSize must be one of 16, 32, 64, 128, 256, 512", op);
+  if (p->kv_heads <= 0 || p->num_heads % p->kv_heads != 0)
+    return fail(CASCADE_ERR_INVALID, "%s: numHeads must be a multiple of kvHeads", op);
+  if (p->num_tokens < 0 || p->batch < 0 || p->num_blocks < 0 || p->block_cols < 0)
+    return fail(CASCADE_ERR_INVALID, "%s: negative size", op);
+  if (p->num_tokens * p->num_heads > (int64_t(1) << 31) / kHeadDim ||
+      p->num_blocks * p->block_size >= (int64_t(1) << 31))
+    return fail(CASCADE_ERR_UNSUPPORTED, "%s: problem too large for 32-bit row indices", op);
+  if (p->q_seqlen_value > 0 && p->num_tokens != p->batch * p->q_seqlen_value)
+    return fail(CASCADE_ERR_INVALID,
+                "%s: with q_seqlen_value=%lld, query.size(0) must equal batch * q_seqlen_value", op,
+                static_cast<long long>(p->q_seqlen_value));
+  return CASCADE_OK;
+}
+
+int validate_pointers(const cascade_paged_attn_t* p, const char* op) {
+  if (p->batch > 0 && p->num_tokens > 0) {
+    if (!p->query || !p->key || !p->value || !p->block_table || !p->actual_q_seqlens || !p->actual_kv_seqlens)
+      return fail(CASCADE_ERR_INVALID, "%s: null device pointer", op);
+    if ((reinterpret_cast<uintptr_t>(p->key) | reinterpret_cast<uintptr_t>(p->value)) & 15)
+      return fail(CASCADE_ERR_INVALID, "%s: key/value must be 16-byte aligned", op);
+    if (reinterpret_cast<uintptr_t>(p->query) & 3)
+      return fail(CASCADE_ERR_INVALID, "%s: query must be 4-byte aligned", op);
+  }
+  return CASCADE_OK;
+}
+
+// Legacy path: read the seqlens back and apply the reference's host checks
+// (op_host/fa_fp32_stage1.cpp:223-241). `allow_zero_kv` relaxes kv >= 1.
+int read_and_check_seqlens(const cascade_paged_attn_t* p, const char* op, bool allow_zero_kv, cudaStream_t stream,
+                           int64_t* max_q) {
+  std::vector<int64_t> q(p->batch), kv(p->batch);
+  cudaError_t e = cudaMemcpyAsync(q.data(), p->actual_q_seqlens, p->batch * sizeof(int64_t),
+                                  cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(kv.data(), p->actual_kv_seqlens, p->batch * sizeof(int64_t), cudaMemcpyDeviceToHost,
+                        stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(op, e);
+  int64_t sum_q = 0, mq = 0, mkv = 0;
+  for (int64_t b = 0; b < p->batch; ++b) {
+    if (q[b] < 1 || kv[b] < (allow_zero_kv ? 0 : 1))
+      return fail(CASCADE_ERR_INVALID, "%s: seqlens must be >= 1", op);
+    sum_q += q[b];
+    mq = std::max(mq, q[b]);
+    mkv = std::max(mkv, kv[b]);
+  }
+  if (sum_q != p->num_tokens)
+    return fail(CASCADE_ERR_INVALID, "%s: query.size(0) must equal sum(actual_q_seqlens)", op);
+  if (ceil_div(mkv, p->block_size) > p->block_cols)
+    return fail(CASCADE_ERR_INVALID, "%s: block_table cols too small for max kv seqlen", op);
+  *max_q = mq;
+  return CASCADE_OK;
+}
+
+int run_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, void* out, float* lse, void* ws,
+              size_t ws_bytes, cudaStream_t stream) {
+  int rc = validate_paged(p, op);
+  if (rc == CASCADE_OK) rc = validate_pointers(p, op);
+  if (rc) return rc;
+  if (p->batch == 0 || p->num_tokens == 0) return CASCADE_OK;
+  if (!out || !lse) return fail(CASCADE_ERR_INVALID, "%s: null output pointer", op);
+  int64_t max_q = p->q_seqlen_value;
+  if (p->q_seqlen_value == 0) {
+    rc = read_and_check_seqlens(p, op, suffix, stream, &max_q);
+    if (rc) return rc;
+  }
+  cascade_attn_plan_t plan;
+  rc = cascade_plan_paged_attn(p, max_q, suffix ? 1 : 0, &plan);
+  if (rc) return rc;
+  if (plan.num_splits > 1) {
+    if (ws == nullptr || ws_bytes < plan.workspace_bytes)
+      return fail(CASCADE_ERR_WORKSPACE, "%s: workspace of %zu bytes required, %zu given", op,
+                  plan.workspace_bytes, ws_bytes);
+    if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(CASCADE_ERR_INVALID, "%s: workspace must be 16-byte aligned", op);
+  }
+
+  PagedAttnLaunch L;
+  std::memset(&L, 0, sizeof(L));
+  const bool tc = plan.kernel == 1;
+  const uint32_t box_rows = static_cast<uint32_t>(std::min<int64_t>(p->block_size, tc ? 128 : 64));
+  const uint64_t inner = static_cast<uint64_t>(p->kv_heads) * kHeadDim;
+  const uint64_t rows = static_cast<uint64_t>(p->num_blocks) * p->block_size;
+  if (rows == 0) return fail(CASCADE_ERR_INVALID, "%s: empty KV pool", op);
+  if (!encode_tmap_2d(&L.tmap_k, p->key, inner, rows, inner * 2, 64, box_rows, true,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
+      !encode_tmap_2d(&L.tmap_v, p->value, inner, rows, inner * 2, 64, box_rows, true,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+    return fail(CASCADE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed", op);
+  L.query = p->query;
+  L.block_table = p->block_table;
+  L.q_seqlens = p->actual_q_seqlens;
+  L.kv_seqlens = p->actual_kv_seqlens;
+  L.out = out;
+  L.lse = lse;
+  const size_t nrows = static_cast<size_t>(p->num_tokens) * p->num_heads;
+  L.part_o = static_cast<float*>(ws);
+  L.part_lse = ws ? static_cast<float*>(ws) + static_cast<size_t>(plan.num_splits) * nrows * kHeadDim : nullptr;
+  L.num_tokens = static_cast<int32_t>(p->num_tokens);
+  L.num_heads = static_cast<int32_t>(p->num_heads);
+  L.kv_heads = static_cast<int32_t>(p->kv_heads);
+  L.group = static_cast<int32_t>(p->num_heads / p->kv_heads);
+  L.batch = static_cast<int32_t>(p->batch);
+  L.block_cols = static_cast<int32_t>(p->block_cols);
+  L.block_size = static_cast<int32_t>(p->block_size);
+  L.num_blocks = static_cast<int32_t>(p->num_blocks);
+  L.q_seqlen_value = static_cast<int32_t>(p->q_seqlen_value);
+  L.max_q_seqlen = static_cast<int32_t>(max_q);
+  L.split_tokens = static_cast<int32_t>(plan.split_tokens);
+  L.num_splits = static_cast<int32_t>(plan.num_splits);
+  L.out_dtype = suffix ? p->dtype : CASCADE_FP32;
+  L.lse_stride = suffix ? 1 : 8;
+  L.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(kHeadDim)) * 1.4426950408889634);
+
+  const bool fp16 = p->dtype == CASCADE_FP16;
+  cudaError_t e = tc ? launch_paged_prefix_tc(L, fp16, stream) : launch_paged_decode(L, fp16, stream);
+  if (e == cudaSuccess && plan.num_splits > 1) e = launch_split_combine(L, stream);
+  if (e != cudaSuccess) return cuda_fail(op, e);
+  return CASCADE_OK;
+}
+
+}  // namespace
+
+bool encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                    uint32_t box_inner, uint32_t box_rows, bool swizzle128, CUtensorMapL2promotion promo) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, promo,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace cascade
+
+using namespace cascade;
+
+extern "C" {
+
+const char* cascade_last_error(void) { return g_last_error.c_str(); }
+
+int cascade_version(void) { return 100; }
+
+int cascade_device_error(uint32_t* word) {
+  unsigned int v = 0, zero = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_cascade_device_error, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_cascade_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return cuda_fail("cascade_device_error", e);
+  if (word) *word = v;
+  return CASCADE_OK;
+}
+
+int cascade_plan_paged_attn(const cascade_paged_attn_t* p, int64_t max_q_seqlen, int32_t suffix_mode,
+                            cascade_attn_plan_t* plan) {
+  const char* op = suffix_mode ? "cascade_suffix_decode" : "fa_fp32_stage1";
+  int rc = validate_paged(p, op);
+  if (rc) return rc;
+  if (!plan) return fail(CASCADE_ERR_INVALID, "%s: null plan", op);
+  const int64_t group = p->num_heads / p->kv_heads;
+  const int64_t rows = std::max<int64_t>(1, max_q_seqlen) * group;
+  plan->kernel = rows <= 16 ? 0 : 1;
+  plan->rows_per_group = static_cast<int32_t>(std::min<int64_t>(rows, INT32_MAX));
+  split_rule(p, plan->kernel, &plan->split_tokens, &plan->num_splits);
+  plan->workspace_bytes = workspace_for(p, plan->num_splits);
+  return CASCADE_OK;
+}
+
+static size_t workspace_size_any(const cascade_paged_attn_t* p, int suffix) {
+  if (validate_paged(p, suffix ? "cascade_suffix_decode" : "fa_fp32_stage1")) return 0;
+  if (p->batch == 0 || p->num_tokens == 0) return 0;
+  if (p->q_seqlen_value > 0) {
+    cascade_attn_plan_t plan;
+    if (cascade_plan_paged_attn(p, p->q_seqlen_value, suffix, &plan)) return 0;
+    return plan.workspace_bytes;
+  }
+  // per-request q lengths: the kernel is chosen after reading them, so size
+  // for whichever kernel needs more
+  size_t best = 0;
+  for (int k = 0; k < 2; ++k) {
+    int64_t st, ns;
+    split_rule(p, k, &st, &ns);
+    best = std::max(best, workspace_for(p, ns));
+  }
+  return best;
+}
+
+size_t cascade_fa_fp32_stage1_workspace_size(const cascade_paged_attn_t* p) { return workspace_size_any(p, 0); }
+
+size_t cascade_suffix_decode_workspace_size(const cascade_paged_attn_t* p) { return workspace_size_any(p, 1); }
+
+int cascade_fa_fp32_stage1(const cascade_paged_attn_t* p, float* out, float* lse, void* workspace,
+                           size_t workspace_bytes, cascade_stream_t stream) {
+  return run_paged(p, "fa_fp32_stage1", false, out, lse, workspace, workspace_bytes,
+                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cascade_suffix_decode(const cascade_paged_attn_t* p, void* out, float* lse, void* workspace,
+                          size_t workspace_bytes, cascade_stream_t stream) {
+  return run_paged(p, "cascade_suffix_decode", true, out, lse, workspace, workspace_bytes,
+                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cascade_lse_merge(const void* o1, int32_t o1_dtype, const void* o2, int32_t o2_dtype, const float* lse1,
+                      int64_t stride1, const float* lse2, int64_t stride2, void* out, int32_t out_dtype,
+                      int64_t rows, int64_t dim, cascade_stream_t stream) {
+  const char* op = "lse_merge";
+  auto dt_ok = [](int32_t d) { return d == CASCADE_BF16 || d == CASCADE_FP16 || d == CASCADE_FP32; };
+  if (!dt_ok(o1_dtype) || !dt_ok(o2_dtype) || !dt_ok(out_dtype))
+    return fail(CASCADE_ERR_INVALID, "%s: dtypes must be bf16, fp16 or fp32", op);
+  if (dim <= 0 || dim % 16 != 0)
+    return fail(CASCADE_ERR_INVALID, "%s: head dim must be a multiple of 16 (MTE 32B alignment)", op);
+  if (rows < 0) return fail(CASCADE_ERR_INVALID, "%s: negative row count", op);
+  if (rows == 0) return CASCADE_OK;
+  if (stride1 < 1 || stride1 > 64 || stride2 < 1 || stride2 > 64)
+    return fail(CASCADE_ERR_INVALID, "%s: lse row stride must be in [1, 64]", op);
+  if (!o1 || !o2 || !lse1 || !lse2 || !out) return fail(CASCADE_ERR_INVALID, "%s: null pointer", op);
+  if ((reinterpret_cast<uintptr_t>(o1) | reinterpret_cast<uintptr_t>(o2) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(CASCADE_ERR_INVALID, "%s: o1/o2/out must be 16-byte aligned", op);
+  LseMergeLaunch L;
+  L.o1 = o1;
+  L.o2 = o2;
+  L.lse1 = lse1;
+  L.lse2 = lse2;
+  L.out = out;
+  L.rows = rows;
+  L.dim = static_cast<int32_t>(dim);
+  L.stride1 = static_cast<int32_t>(stride1);
+  L.stride2 = static_cast<int32_t>(stride2);
+  L.o1_dtype = o1_dtype;
+  L.o2_dtype = o2_dtype;
+  L.out_dtype = out_dtype;
+  cudaError_t e = launch_lse_merge(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(op, e);
+  return CASCADE_OK;
+}
+
+int cascade_f3_gateup_epilogue(const void* a, const void* b, void* ws, void* d, int64_t d_stride, int64_t M,
+                               int64_t K, int64_t I, int32_t mode, cascade_stream_t stream) {
+  const char* op = "f3_gateup_epilogue";
+  if (!((mode >= 0 && mode <= 5) || mode == 7 || mode == 8))
+    return fail(CASCADE_ERR_INVALID, "%s: mode must be 0..5, 7 or 8", op);
+  if (M <= 0 || K <= 0) return fail(CASCADE_ERR_INVALID, "%s: empty input", op);
+  if (K % 16 != 0) return fail(CASCADE_ERR_INVALID, "%s: K must be a multiple of 16", op);
+  if (I <= 0 || I % 128 != 0) return fail(CASCADE_ERR_INVALID, "%s: I must be a multiple of the N tile", op);
+  if (K < 64) return fail(CASCADE_ERR_INVALID, "%s: K must be >= 64 (L0 K tile)", op);
+  if (M > INT32_MAX || K > INT32_MAX || I > INT32_MAX / 2)
+    return fail(CASCADE_ERR_UNSUPPORTED, "%s: dimension too large", op);
+  const bool needs_ws = mode != 1;
+  const bool needs_d = mode != 2 && mode != 7;
+  if (needs_ws && !ws) return fail(CASCADE_ERR_WORKSPACE, "%s: workspace must be contiguous bf16 [M, 2I]", op);
+  if (needs_d && (!d || d_stride < I)) return fail(CASCADE_ERR_INVALID, "%s: d must be bf16 [M, I]", op);
+  if (needs_d && (d_stride % 8 != 0 || (reinterpret_cast<uintptr_t>(d) & 15)))
+    return fail(CASCADE_ERR_INVALID, "%s: d must be 16-byte aligned with a row stride multiple of 8", op);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (mode == 3 || mode == 5 || mode == 7 || mode == 8) {
+    cudaError_t e = launch_gateup_window(ws, d, d_stride, static_cast<int32_t>(M), static_cast<int32_t>(I), mode, st);
+    if (e != cudaSuccess) return cuda_fail(op, e);
+    return CASCADE_OK;
+  }
+  if (!a || !b) return fail(CASCADE_ERR_INVALID, "%s: null input", op);
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15)
+    return fail(CASCADE_ERR_INVALID, "%s: a/b must be 16-byte aligned", op);
+  GateUpLaunch L;
+  std::memset(&L, 0, sizeof(L));
+  L.ws = ws;
+  L.d = d;
+  L.d_stride = d_stride;
+  L.M = static_cast<int32_t>(M);
+  L.K = static_cast<int32_t>(K);
+  L.I = static_cast<int32_t>(I);
+  L.mode = mode;
+  cudaError_t e = launch_gateup(L, a, b, st);
+  if (e != cudaSuccess) return cuda_fail(op, e);
+  return CASCADE_OK;
+}
+
+}  // extern "C"

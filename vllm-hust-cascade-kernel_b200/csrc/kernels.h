@@ -1,0 +1,82 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace cascade {
+
+constexpr int kHeadDim = 128;
+constexpr int kNumSMs = 148;
+
+// ----------------------------------------------------------------------------
+// paged attention (decode path: <= 16 query rows per (request, kv head))
+// ----------------------------------------------------------------------------
+struct PagedAttnLaunch {
+  CUtensorMap tmap_k;  // 2-D view [num_blocks*block_size, kv_heads*128], box {64, box_rows}, SW128
+  CUtensorMap tmap_v;
+  const void* query;
+  const int32_t* block_table;
+  const int64_t* q_seqlens;
+  const int64_t* kv_seqlens;
+  void* out;            // final output (nsplit == 1) in out_dtype
+  float* lse;           // final lse (nsplit == 1), row stride lse_stride
+  float* part_o;        // [nsplit][T*H][128] fp32 (nsplit > 1)
+  float* part_lse;      // [nsplit][T*H]
+  int32_t num_tokens, num_heads, kv_heads, group;
+  int32_t batch, block_cols, block_size, num_blocks;
+  int32_t q_seqlen_value;  // > 0 uniform, 0 = per-request (prefix-summed in kernel)
+  int32_t max_q_seqlen;
+  int32_t split_tokens, num_splits;
+  int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
+  int32_t lse_stride;   // 8 (reference padded rows) or 1 (compact)
+  float scale_log2;     // softmax scale * log2(e)
+};
+
+cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream);
+
+// Stage-1 tensor-core path (tcgen05, > 16 rows per (request, kv head)).
+cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream);
+
+// Merge the nsplit partials of every (token, head) row into the final output.
+cudaError_t launch_split_combine(const PagedAttnLaunch& p, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------
+// LSE merge
+// ----------------------------------------------------------------------------
+struct LseMergeLaunch {
+  const void* o1;
+  const void* o2;
+  const float* lse1;
+  const float* lse2;
+  void* out;
+  int64_t rows;
+  int32_t dim;
+  int32_t stride1, stride2;
+  int32_t o1_dtype, o2_dtype, out_dtype;  // 0 bf16, 1 fp16, 2 fp32
+};
+
+cudaError_t launch_lse_merge(const LseMergeLaunch& p, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------
+// gate_up GEMM + epilogue
+// ----------------------------------------------------------------------------
+struct GateUpLaunch {
+  void* ws;            // [M, 2I] bf16 (modes that write C)
+  void* d;             // [M, I] bf16
+  int64_t d_stride;
+  int32_t M, K, I;
+  int32_t mode;
+};
+
+cudaError_t launch_gateup(const GateUpLaunch& p, const void* a, const void* b, cudaStream_t stream);
+// Modes 3/5/7/8: epilogue window traffic on an existing workspace (no GEMM).
+cudaError_t launch_gateup_window(const void* ws, void* d, int64_t d_stride, int32_t M, int32_t I, int32_t mode,
+                                 cudaStream_t stream);
+
+// Host: encode a 2-D bf16/fp16 tiled tensor map (SW128 when inner box is 64).
+bool encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                    uint32_t box_inner, uint32_t box_rows, bool swizzle128, CUtensorMapL2promotion promo);
+
+}  // namespace cascade

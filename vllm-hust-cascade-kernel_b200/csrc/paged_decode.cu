@@ -1,0 +1,435 @@
+// Paged decode attention for the cascade: <= 16 query rows per (request, kv
+// head) -- the per-request suffix stage (q_len = 1, GQA group <= 16) and the
+// small-row forms of the stage-1 op.
+//
+// Memory-bound design (KV bytes dominate):
+//  * one CTA per (split of 256 kv tokens, kv head, request); the split's
+//    partial (O, LSE) is merged by launch_split_combine when a request has
+//    more than one split;
+//  * a producer warp streams 64-token K/V tiles with 2-D TMA (one box per page
+//    segment and 64-element half of the head dim, 128-byte swizzle) into a
+//    3-stage ring: 32 KB per stage, 96 KB per CTA, two CTAs per SM;
+//  * four consumer warps each own 16 tokens of every tile: QK^T and PV with
+//    m16n8k16 mma.sync (rows = the <= 16 query rows of the GQA group), P kept
+//    in registers (fp32 -> 16-bit RNE, the reference's quantisation point,
+//    kernel_fa_fp32_stage1.cpp / block_epilogue_online_softmax_no_mask.hpp:578-591),
+//    row sums from the unquantised fp32 exps, warp-shuffle row reductions;
+//  * the 4 warps' (m, l, O) are merged through shared memory at the end.
+// Each warp runs its own online softmax over its tokens in 16-token steps;
+// the CPU oracle reproduces this structure exactly (chunk 16, segments =
+// the warp's token subsets).
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace cascade {
+
+namespace {
+
+constexpr int kTile = 64;              // kv tokens per pipeline stage
+constexpr int kStages = 3;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kHalfBytes = kTile * 128;          // one [64 tokens x 64 dims] 16-bit box region
+constexpr int kKBytes = 2 * kHalfBytes;           // K tile, both dim halves
+constexpr int kStageBytes = 2 * kKBytes;          // K + V
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+struct __align__(8) DecodeBarriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+};
+
+__device__ __forceinline__ int request_token_offset(const PagedAttnLaunch& p, int b) {
+  if (p.q_seqlen_value > 0) return b * p.q_seqlen_value;
+  // per-request q lengths: prefix sum over the first b entries (warp-parallel)
+  int lane = threadIdx.x & 31;
+  long long acc = 0;
+  for (int i = lane; i < b; i += 32) acc += p.q_seqlens[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  return static_cast<int>(acc);
+}
+
+template <bool kFp16>
+__device__ __forceinline__ void store_out(void* out, int out_dtype, size_t idx, float v0, float v1) {
+  if (out_dtype == 2) {
+    *reinterpret_cast<float2*>(static_cast<float*>(out) + idx) = make_float2(v0, v1);
+  } else if (out_dtype == 1) {
+    *reinterpret_cast<__half2*>(static_cast<__half*>(out) + idx) = __floats2half2_rn(v0, v1);
+  } else {
+    *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(out) + idx) = __floats2bfloat162_rn(v0, v1);
+  }
+}
+
+template <bool kFp16>
+__global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_constant__ PagedAttnLaunch p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DecodeBarriers* bars = reinterpret_cast<DecodeBarriers*>(smem + kStages * kStageBytes);
+
+  const int split = blockIdx.x;
+  const int g = blockIdx.y;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int kv = static_cast<int>(p.kv_seqlens[b]);
+  const int q_len = p.q_seqlen_value > 0 ? p.q_seqlen_value : static_cast<int>(p.q_seqlens[b]);
+  const int nrows = q_len * p.group;
+  const int tok0 = request_token_offset(p, b);
+  const int s_begin = split * p.split_tokens;
+  const int s_end = min(kv, s_begin + p.split_tokens);
+  const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
+
+  // Empty split (kv shorter than this split's start, or no query rows):
+  // write -inf partials so the combine step skips it.
+  if (ntiles == 0 || nrows == 0) {
+    if (p.num_splits > 1) {
+      for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
+        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+        p.part_lse[static_cast<size_t>(split) * p.num_tokens * p.num_heads + static_cast<size_t>(t) * p.num_heads + h] =
+            -INFINITY;
+      }
+    } else {
+      // single split: kv == 0 -> out = 0, lse = -inf
+      for (int i = threadIdx.x; i < nrows * kHeadDim / 2; i += blockDim.x) {
+        int r = i / (kHeadDim / 2), d = (i % (kHeadDim / 2)) * 2;
+        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+        store_out<kFp16>(p.out, p.out_dtype, (static_cast<size_t>(t) * p.num_heads + h) * kHeadDim + d, 0.f, 0.f);
+      }
+      for (int i = threadIdx.x; i < nrows * p.lse_stride; i += blockDim.x) {
+        int r = i / p.lse_stride, c = i % p.lse_stride;
+        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+        p.lse[(static_cast<size_t>(t) * p.num_heads + h) * p.lse_stride + c] = -INFINITY;
+      }
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tmap_k);
+      tma_prefetch_desc(&p.tmap_v);
+      const int bs = p.block_size;
+      const int box_rows = bs < kTile ? bs : kTile;
+      const int oob_row = p.num_blocks * bs;  // fully out of range -> zero fill
+      const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
+      const int npages = (kv + bs - 1) / bs;
+      for (int i = 0; i < ntiles; ++i) {
+        const int st = i % kStages;
+        if (i >= kStages) mbar_wait(&bars->empty[st], ((i / kStages) - 1) & 1);
+        uint8_t* sk = smem + st * kStageBytes;
+        uint8_t* sv = sk + kKBytes;
+        mbar_arrive_expect_tx(&bars->full[st], kStageBytes);
+        const int t_tile = s_begin + i * kTile;
+        for (int off = 0; off < kTile; off += box_rows) {
+          const int t = t_tile + off;
+          const int page = t / bs;
+          int row;
+          if (page < npages) {
+            row = bt[page] * bs + (t % bs);
+          } else {
+            row = oob_row;
+          }
+          const int x0 = g * kHeadDim;
+          uint8_t* dk = sk + off * 128;
+          uint8_t* dv = sv + off * 128;
+          tma_load_2d(dk, &p.tmap_k, &bars->full[st], x0, row);
+          tma_load_2d(dk + kHalfBytes, &p.tmap_k, &bars->full[st], x0 + 64, row);
+          tma_load_2d(dv, &p.tmap_v, &bars->full[st], x0, row);
+          tma_load_2d(dv + kHalfBytes, &p.tmap_v, &bars->full[st], x0 + 64, row);
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int gq = lane >> 2;  // fragment row group (0..7)
+  const int tq = lane & 3;   // thread in quad
+
+  // Q A-fragments: rows gq and gq+8, 8 k-steps over the 128 dims.
+  uint32_t qa[8][4];
+  {
+    const uint16_t* q = static_cast<const uint16_t*>(p.query);
+    const int rows[2] = {gq, gq + 8};
+    uint32_t v[2][8][2];
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      const int r = rows[ri];
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        v[ri][ks][0] = 0;
+        v[ri][ks][1] = 0;
+      }
+      if (r < nrows) {
+        const int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+        const uint16_t* src = q + (static_cast<size_t>(t) * p.num_heads + h) * kHeadDim;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          v[ri][ks][0] = *reinterpret_cast<const uint32_t*>(src + ks * 16 + 2 * tq);
+          v[ri][ks][1] = *reinterpret_cast<const uint32_t*>(src + ks * 16 + 8 + 2 * tq);
+        }
+      }
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = v[0][ks][0];
+      qa[ks][1] = v[1][ks][0];
+      qa[ks][2] = v[0][ks][1];
+      qa[ks][3] = v[1][ks][1];
+    }
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY;  // running max (log2 units) rows gq, gq+8
+  float l0 = 0.f, l1 = 0.f;              // this thread's share of the row sums
+
+  const uint32_t smem_base = smem_u32(smem);
+  const int wrow = warp * 16;  // this warp's first token row within a tile
+  // ldmatrix row addresses (matrix index = lane / 8, row = lane % 8)
+  const int mi = lane >> 3, mr = lane & 7;
+
+  for (int i = 0; i < ntiles; ++i) {
+    const int st = i % kStages;
+    mbar_wait(&bars->full[st], (i / kStages) & 1);
+    const uint32_t kbase = smem_base + st * kStageBytes;
+    const uint32_t vbase = kbase + kKBytes;
+
+    // S = Q K^T over this warp's 16 tokens (two n8 tiles)
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      const int trow = wrow + (mi >> 1) * 8 + mr;  // token row of this lane's ldmatrix address
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int dim = ks * 16 + (mi & 1) * 8;
+        const uint32_t addr = kbase + (dim >> 6) * kHalfBytes + sw128(trow, (dim & 63) >> 3);
+        uint32_t r[4];
+        ldmatrix_x4(r, addr);
+        mma_16816<kFp16>(s[0], qa[ks], r[0], r[1]);
+        mma_16816<kFp16>(s[1], qa[ks], r[2], r[3]);
+      }
+    }
+
+    // mask tokens beyond kv, scale to log2 units, online softmax
+    const int tbase = s_begin + i * kTile + wrow;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const int tk = tbase + n * 8 + 2 * tq;
+      s[n][0] = (tk < s_end) ? s[n][0] * p.scale_log2 : -INFINITY;
+      s[n][1] = (tk + 1 < s_end) ? s[n][1] * p.scale_log2 : -INFINITY;
+      s[n][2] = (tk < s_end) ? s[n][2] * p.scale_log2 : -INFINITY;
+      s[n][3] = (tk + 1 < s_end) ? s[n][3] * p.scale_log2 : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(s[n][0], s[n][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[n][2], s[n][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float ms0 = mn0 == -INFINITY ? 0.f : mn0;  // all-masked-so-far guard
+    const float ms1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = m0 == -INFINITY ? 0.f : ex2(m0 - ms0);
+    const float al1 = m1 == -INFINITY ? 0.f : ex2(m1 - ms1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      s[n][0] = ex2(s[n][0] - ms0);
+      s[n][1] = ex2(s[n][1] - ms0);
+      s[n][2] = ex2(s[n][2] - ms1);
+      s[n][3] = ex2(s[n][3] - ms1);
+      ps0 += s[n][0] + s[n][1];
+      ps1 += s[n][2] + s[n][3];
+    }
+    l0 = al0 * l0 + ps0;
+    l1 = al1 * l1 + ps1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= al0;
+      o[n][1] *= al0;
+      o[n][2] *= al1;
+      o[n][3] *= al1;
+    }
+    // P (16-bit, RNE) as the A operand of PV: C-fragment layout == A layout
+    uint32_t pa[4];
+    pa[0] = pack2<kFp16>(s[0][0], s[0][1]);
+    pa[1] = pack2<kFp16>(s[0][2], s[0][3]);
+    pa[2] = pack2<kFp16>(s[1][0], s[1][1]);
+    pa[3] = pack2<kFp16>(s[1][2], s[1][3]);
+
+    {
+      const int trow = wrow + (mi & 1) * 8 + mr;
+#pragma unroll
+      for (int pp = 0; pp < 8; ++pp) {
+        const int dim = pp * 16 + (mi >> 1) * 8;
+        const uint32_t addr = vbase + (dim >> 6) * kHalfBytes + sw128(trow, (dim & 63) >> 3);
+        uint32_t r[4];
+        ldmatrix_x4_trans(r, addr);
+        mma_16816<kFp16>(o[2 * pp], pa, r[0], r[1]);
+        mma_16816<kFp16>(o[2 * pp + 1], pa, r[2], r[3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->empty[st]);
+  }
+
+  // row sums over the quad
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  // --------------------------------------------- merge the 4 warps in smem
+  // All tiles are consumed (every full barrier was waited by every warp), so
+  // the stage ring is free once all consumer warps reach this barrier.
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  float* so = reinterpret_cast<float*>(smem);                 // [4][16][128]
+  float* sm = so + kConsumerWarps * 16 * kHeadDim;            // [4][16]
+  float* sl = sm + kConsumerWarps * 16;                       // [4][16]
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const int d = n * 8 + 2 * tq;
+    *reinterpret_cast<float2*>(&so[(warp * 16 + gq) * kHeadDim + d]) = make_float2(o[n][0], o[n][1]);
+    *reinterpret_cast<float2*>(&so[(warp * 16 + gq + 8) * kHeadDim + d]) = make_float2(o[n][2], o[n][3]);
+  }
+  if (tq == 0) {
+    sm[warp * 16 + gq] = m0;
+    sm[warp * 16 + gq + 8] = m1;
+    sl[warp * 16 + gq] = l0;
+    sl[warp * 16 + gq + 8] = l1;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+
+  // 128 threads: thread -> (row = tid / 8, 16 dims); 16 rows x 8 threads
+  const int tid = threadIdx.x;
+  const int r = tid >> 3;
+  const int d0 = (tid & 7) * 16;
+  if (r < nrows) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm[w * 16 + r]);
+    float wsum = 0.f, wt[kConsumerWarps];
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float mw = sm[w * 16 + r];
+      wt[w] = (mw == -INFINITY) ? 0.f : ex2(mw - M);
+      wsum += wt[w] * sl[w * 16 + r];
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    const float lse_nat = (wsum > 0.f) ? (M + log2f(wsum)) * 0.6931471805599453f : -INFINITY;
+    const int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+    const size_t row = static_cast<size_t>(t) * p.num_heads + h;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      if (wt[w] == 0.f) continue;
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(&so[(w * 16 + r) * kHeadDim + d0 + j]);
+        acc[j] += wt[w] * v.x;
+        acc[j + 1] += wt[w] * v.y;
+        acc[j + 2] += wt[w] * v.z;
+        acc[j + 3] += wt[w] * v.w;
+      }
+    }
+    if (p.num_splits > 1) {
+      float* dst = p.part_o + (static_cast<size_t>(split) * p.num_tokens * p.num_heads + row) * kHeadDim + d0;
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(dst + j) =
+            make_float4(acc[j] * inv, acc[j + 1] * inv, acc[j + 2] * inv, acc[j + 3] * inv);
+      if ((tid & 7) == 0) p.part_lse[static_cast<size_t>(split) * p.num_tokens * p.num_heads + row] = lse_nat;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; j += 2)
+        store_out<kFp16>(p.out, p.out_dtype, row * kHeadDim + d0 + j, acc[j] * inv, acc[j + 1] * inv);
+      if ((tid & 7) < p.lse_stride) {
+        for (int c = tid & 7; c < p.lse_stride; c += 8) p.lse[row * p.lse_stride + c] = lse_nat;
+      }
+    }
+  }
+}
+
+// One warp per (token, head) row: merge the split partials.
+__global__ void split_combine_kernel(const __grid_constant__ PagedAttnLaunch p) {
+  const int warps_per_block = blockDim.x >> 5;
+  const size_t row = static_cast<size_t>(blockIdx.x) * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const size_t rows = static_cast<size_t>(p.num_tokens) * p.num_heads;
+  if (row >= rows) return;
+  const size_t plane = rows;
+  float M = -INFINITY;
+  for (int s = 0; s < p.num_splits; ++s) M = fmaxf(M, p.part_lse[s * plane + row]);
+  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f, wsum = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < p.num_splits; ++s) {
+      const float l = p.part_lse[s * plane + row];
+      if (l == -INFINITY) continue;
+      const float w = __expf(l - M);
+      const float4 v = *reinterpret_cast<const float4*>(p.part_o + (s * plane + row) * kHeadDim + lane * 4);
+      acc0 += w * v.x;
+      acc1 += w * v.y;
+      acc2 += w * v.z;
+      acc3 += w * v.w;
+      wsum += w;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const float lse = wsum > 0.f ? M + __logf(wsum) : -INFINITY;
+  const size_t o = row * kHeadDim + lane * 4;
+  if (p.out_dtype == 2) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p.out) + o) =
+        make_float4(acc0 * inv, acc1 * inv, acc2 * inv, acc3 * inv);
+  } else if (p.out_dtype == 1) {
+    __half2 a = __floats2half2_rn(acc0 * inv, acc1 * inv), c = __floats2half2_rn(acc2 * inv, acc3 * inv);
+    uint2 u = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&c));
+    *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + o) = u;
+  } else {
+    __nv_bfloat162 a = __floats2bfloat162_rn(acc0 * inv, acc1 * inv), c = __floats2bfloat162_rn(acc2 * inv, acc3 * inv);
+    uint2 u = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&c));
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + o) = u;
+  }
+  if (lane < p.lse_stride) {
+    for (int c = lane; c < p.lse_stride; c += 32) p.lse[row * p.lse_stride + c] = lse;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream) {
+  dim3 grid(p.num_splits, p.kv_heads, p.batch);
+  auto kern = fp16 ? paged_decode_kernel<true> : paged_decode_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_combine(const PagedAttnLaunch& p, cudaStream_t stream) {
+  const size_t rows = static_cast<size_t>(p.num_tokens) * p.num_heads;
+  const int wpb = 8;
+  const unsigned blocks = static_cast<unsigned>((rows + wpb - 1) / wpb);
+  if (blocks == 0) return cudaSuccess;
+  split_combine_kernel<<<blocks, wpb * 32, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace cascade
