@@ -1,0 +1,378 @@
+"""Cascade-decode benchmark (BASELINE metric: cascade decode attention HBM GB/s
+and us/step on the Llama-3-8B-shaped cascade, plus the SwiGLU gate_up line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one cascade decode step of one layer on synthetic inputs with the
+config's shapes (B=64 requests sharing a 4096-token prefix, suffix lengths
+U[128,1024], 32 q heads / 8 kv heads, head dim 128, block size 128, bf16,
+random-permutation block tables): stage-1 prefix attention over the shared
+pages, per-request suffix decode, LSE merge to the bf16 output.
+
+Multi-GPU (torchrun, one rank per GPU): attention is partitioned by kv head
+with no hot-path collective, so every rank owns 8 kv heads / 32 q heads of a
+model with 8N kv heads (weak scaling); NCCL is used only for the barrier and
+the max-over-ranks timing.
+
+``value`` = algorithmic bytes of all ranks / max-over-ranks device time.
+L2 is flushed (a 256 MiB write) before every timed step; each step is timed
+with CUDA events on the launching stream.  ``e2e`` repeats the step through
+the public op with host buffers: q and the tables copied from pinned host
+memory and the output copied back inside the timed region.
+``--impl reference`` times the reference's CPU golden path (its numpy fp64
+restatement in oracle/) on the host cores, on rank 0 only.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "vllm-hust-cascade-kernel_b200"))
+
+METRIC = "cascade decode attention HBM GB/s (Llama-3-8B cascade step, B=64, prefix 4096)"
+FLUSH_BYTES = 256 * 1024 * 1024
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except Exception:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def setup_dist():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    import torch
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- ours
+
+def run_ours(args, rank, world, local):
+    import torch
+    import cascade_kernel  # noqa: F401  (registers the ops; fails loudly if unbuilt)
+    from cascade_kernel import capi, workloads
+    from cascade_kernel.cascade import cascade_decode
+
+    npu = torch.ops.npu
+    peaks = _peaks()
+    w = workloads.c2_llama8b(seed=args.seed + 1000 * rank)
+    t = w.tables
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    ab = w.algorithmic_bytes()
+
+    def step():
+        return cascade_decode(w.q, w.k_pool, w.v_pool, t)
+
+    def suffix_op():
+        return npu.cascade_suffix_decode(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens,
+                                         t.suffix_kv_seqlens, 1)
+
+    # launches per step (the planner tells how many split-combine kernels run)
+    def n_launches():
+        d1 = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.prefix_block_table, t.prefix_q_seqlens,
+                             t.prefix_kv_seqlens, t.uniform_group)
+        d2 = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens,
+                             t.suffix_kv_seqlens, 1)
+        p1 = capi.plan(d1, t.uniform_group, False)
+        p2 = capi.plan(d2, 1, True)
+        return (1 + (p1.num_splits > 1)) + (1 + (p2.num_splits > 1)) + 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            e0, e1, e2, e3 = ev[i]
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            flush.zero_()
+            e2.record(stream)
+            suffix_op()          # the dominant kernel, timed on its own stream position
+            e3.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    step_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    dom_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
+    step_ms = max_over_ranks(step_ms, world)
+    dom_ms = max_over_ranks(dom_ms, world)
+
+    # e2e through the public op with host buffers
+    q_h = w.q.cpu().pin_memory()
+    tabs = [t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens, t.suffix_block_table,
+            t.suffix_q_seqlens, t.suffix_kv_seqlens]
+    tabs_h = [x.cpu().pin_memory() for x in tabs]
+    out_h = torch.empty(w.q.shape, dtype=torch.bfloat16).pin_memory()
+    q_d = torch.empty_like(w.q)
+    tabs_d = [torch.empty_like(x) for x in tabs]
+    from cascade_kernel.cascade import CascadeTables
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        for d_, h_ in zip(tabs_d, tabs_h):
+            d_.copy_(h_, non_blocking=True)
+        tt = CascadeTables(*tabs_d, uniform_group=t.uniform_group)
+        out = cascade_decode(q_d, w.k_pool, w.v_pool, tt)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    for i in range(args.steps):
+        flush.zero_()
+        e2e_ev[i][0].record(stream)
+        e2e_step()
+        e2e_ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_ev) / args.steps, world)
+    h2d = q_h.numel() * q_h.element_size() + sum(x.numel() * x.element_size() for x in tabs_h)
+    d2h = out_h.numel() * out_h.element_size()
+
+    total_bytes = ab["total"] * world
+    value = total_bytes / (step_ms * 1e-3) / 1e9
+    dom_bytes = ab["suffix"]
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, args.cpu_threads)
+
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 5),
+        "us_per_step": round(step_ms * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v, random-permutation block tables)",
+        "config": {
+            "workload": "c2_llama3_8b_cascade: B=64, shared prefix 4096, suffix U[128,1024], "
+                        "H=32/KVH=8 per rank, D=128, block_size=128",
+            "suffix_tokens": int(w.suffix_lens.sum()),
+            "algorithmic_bytes_per_step_per_rank": ab,
+            "parallelism": f"kv-head partition x{world} (weak: 8 kv heads per rank)",
+            "l2": "flushed (256 MiB write) before every timed step",
+        },
+        "roofline": {
+            "kernel": "suffix decode op (paged_decode_kernel + split_combine_kernel)",
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4),
+            "traffic": None,
+            "peak_src": peaks["src"],
+        },
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "us_per_step": round(e2e_ms * 1e3, 2), "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": n_launches() * args.steps + 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    line["frac_of_hbm_roofline_step"] = round(value / world / peaks["hbm_gbs"], 4)
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+# ----------------------------------------------------------------- CPU baseline
+
+def _cpu_task(payload):
+    from oracle import cascade_oracle as O
+    (qh, kh, vh, bt_p, gs, pl, bt_s, sl, heads) = payload
+    t0 = time.perf_counter()
+    O.cascade_step_ref(qh, kh, vh, bt_p, gs, pl, bt_s, sl, kv_heads_subset=heads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(w, threads=None, kv_heads=None):
+    """The reference's CPU golden path (numpy fp64, oracle/cascade_oracle.py)
+    on the same workload: the full cascade step (all 8 kv heads) split over a
+    process pool by kv head.  Returns the cpu_baseline object."""
+    import multiprocessing as mp
+    import numpy as np
+    import torch
+    threads = threads or os.cpu_count() or 1
+    kvh = w.k_pool.shape[2]
+    heads = list(range(kvh)) if kv_heads is None else list(kv_heads)
+    f64 = lambda x: x.float().cpu().numpy().astype(np.float64)
+    qh = f64(w.q)
+    # only the pages the step touches travel to the workers
+    bt_p = w.tables.prefix_block_table.cpu().numpy()
+    bt_s = w.tables.suffix_block_table.cpu().numpy()
+    kf, vf = w.k_pool.float().cpu().numpy(), w.v_pool.float().cpu().numpy()
+    payloads = []
+    for g in heads:
+        group = qh.shape[1] // kvh
+        payloads.append((qh[:, g * group:(g + 1) * group], kf[:, :, g:g + 1].astype(np.float64),
+                         vf[:, :, g:g + 1].astype(np.float64), bt_p, w.group_sizes, w.prefix_lens, bt_s,
+                         w.suffix_lens, [0]))
+    workers = min(threads, len(payloads))
+    t0 = time.perf_counter()
+    if workers > 1:
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(workers) as pool:
+            pool.map(_cpu_task, payloads)
+    else:
+        for pl in payloads:
+            _cpu_task(pl)
+    wall = time.perf_counter() - t0
+    ab = w.algorithmic_bytes()["total"] * len(heads) / kvh
+    return {"value": round(ab / wall / 1e9, 4), "unit": "GB/s", "cores": workers, "kind": "port",
+            "sample": f"full C2 cascade step, {len(heads)} of {kvh} kv heads, numpy fp64 oracle "
+                      f"(spawned pool over kv heads), wall {wall:.2f} s",
+            "seconds": round(wall, 3)}
+
+
+def run_reference(args, rank, world):
+    import torch
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "vllm-hust-cascade-kernel_b200"))
+    from cascade_kernel import workloads
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    w = workloads.c2_llama8b(seed=args.seed, device=dev)
+    threads = args.cpu_threads or os.cpu_count() or 1
+    vals, secs = [], []
+    for i in range(args.warmup + args.steps):
+        c = cpu_baseline(w, threads)
+        if i >= args.warmup:
+            vals.append(c["value"])
+            secs.append(c["seconds"])
+    v = sum(vals) / len(vals)
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * sum(secs) / len(secs), 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded)", "config": {"workload": "c2_llama3_8b_cascade (same as ours)"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": c["cores"], "kind": "port",
+                             "sample": c["sample"]},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-threads", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    rank, world, local = setup_dist()
+    line = run_ours(args, rank, world, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -169,7 +169,7 @@ def decode_segments(kv, split=256, tile=64, warps=4):
 
 def paged_attention_ref(q, k, v, block_table, q_seqlens, kv_seqlens, *,
                         chunk=512, split=None, segments=None, p_dtype="bf16", scale=None,
-                        with_tieband=False, tie_band_rel=2e-5):
+                        with_tieband=False, tie_band_rel=2e-5, tieband_rule="reference"):
     """fp64 paged attention with the reference kernel's quantisation points.
 
     Restates fa_fp64_ref (fa_fp32_ref.py:82-126): S = (q.k)*scale; online
@@ -187,6 +187,12 @@ def paged_attention_ref(q, k, v, block_table, q_seqlens, kv_seqlens, *,
     overrides chunk/split with an arbitrary token-to-segment assignment.
 
     q: [T,H,D]; k,v: [numBlocks, bs, KVH, D] (values already on the input grid).
+    ``tieband_rule``: "reference" accumulates the near-tie bound exactly as
+    fa_fp32_ref.py:199-200 (amb += dm * new_term), which is exact for a single
+    chunk but can under-count flips of an earlier chunk once later chunks
+    raise the running max; "rescaled" carries the bound like the accumulator
+    (amb = dm * amb + new_term), the right rule for many small chunks.
+
     Returns (O [T,H,D] f64, LSE [T,H] f64[, A [T,H,D] tie-band bound]).
     kv == 0 -> O = 0, LSE = -inf."""
     q64 = np.asarray(q, dtype=np.float64)
@@ -230,10 +236,12 @@ def paged_attention_ref(q, k, v, block_table, q_seqlens, kv_seqlens, *,
                     p, g_lo, g_hi = _neighbours(ls, p_dtype)
                     mid = 0.5 * (g_lo + g_hi)
                     ambiguous = np.abs(ls - mid) <= tie_band_rel * ls
-                    # accumulated exactly as fa_fp32_ref.py:199-200 does it
-                    # (the step's dm scales the new term, not the old bound)
-                    amb = amb + dm[:, :, None] * np.einsum(
-                        "htk,khd->htd", ambiguous * (g_hi - g_lo), np.abs(vb[idx]))
+                    term = np.einsum("htk,khd->htd", ambiguous * (g_hi - g_lo), np.abs(vb[idx]))
+                    if tieband_rule == "reference":
+                        # fa_fp32_ref.py:199-200: the step's dm scales the new term
+                        amb = amb + dm[:, :, None] * term
+                    else:
+                        amb = dm[:, :, None] * amb + term
                 else:
                     p = quantize(ls, p_dtype)
                 gl = dm * gl + ls.sum(axis=2)
@@ -333,3 +341,35 @@ def gateup_ref_fp64(x, w):
     I = c.shape[1] // 2
     g, u = c[:, :I], c[:, I:]
     return g / (1.0 + np.exp(-g)) * u
+
+
+# ---------------------------------------------------------------------------
+# one cascade decode step (stage-1 prefix + suffix + merge), as the reference's
+# consumer composes it (ascend-kernel/README.md:158-201)
+# ---------------------------------------------------------------------------
+
+def cascade_step_ref(q, k, v, prefix_bt, group_sizes, prefix_lens, suffix_bt, suffix_lens, *,
+                     p_dtype="bf16", out_dtype="bf16", kv_heads_subset=None):
+    """fp64 cascade step.  q [B,H,D]; k/v [NB,bs,KVH,D] (grid values);
+    prefix_bt [G,cols]; suffix_bt [B,cols].  Stage-1 flattens each prefix
+    group's requests into one request of q_len = group size (README.md:174-177);
+    the suffix runs per request with q_len 1; the merge follows
+    lse_merge_cases.py:45-50.  ``kv_heads_subset`` restricts the computation
+    to those kv heads (and their query heads).  Returns (out [B,H',D] rounded
+    to out_dtype, lse [B,H'])."""
+    q = np.asarray(q, np.float64)
+    B, H, D = q.shape
+    KVH = k.shape[2]
+    group = H // KVH
+    if kv_heads_subset is not None:
+        heads = np.concatenate([np.arange(g * group, (g + 1) * group) for g in kv_heads_subset])
+        q = q[:, heads]
+        k = k[:, :, list(kv_heads_subset)]
+        v = v[:, :, list(kv_heads_subset)]
+    o1, l1 = paged_attention_ref(q, k, v, prefix_bt, np.asarray(group_sizes), np.asarray(prefix_lens),
+                                 p_dtype=p_dtype)
+    o2, l2 = paged_attention_ref(q, k, v, suffix_bt, np.ones(B, np.int64), np.asarray(suffix_lens),
+                                 p_dtype=p_dtype)
+    o2 = quantize(o2, p_dtype)          # the suffix output is in the input dtype
+    out, lse = lse_merge_ref(o1, o2, l1, l2)
+    return quantize(out, out_dtype), lse

@@ -49,7 +49,8 @@ def _check_stage1(z, out, lse, q_len_max):
     # exact structure check against the kernel-structured oracle
     qh, kh, vh, bt, qs, kvs = Hh.fixture_host_args(z)
     _, kw = Hh.kernel_structure(q_len_max, H // KVH, None, T, H, KVH, len(qs), bt.shape[1], kh.shape[1])
-    o_ks, l_ks, A = O.paged_attention_ref(qh, kh, vh, bt, qs, kvs, with_tieband=True, **kw)
+    o_ks, l_ks, A = O.paged_attention_ref(qh, kh, vh, bt, qs, kvs, with_tieband=True,
+                                          tieband_rule="rescaled", **kw)
     _assert_within(o, o_ks, A + 3e-6)
     assert np.abs(l - l_ks).max() < 1e-5
 
@@ -127,7 +128,7 @@ def test_suffix_decode_block_sizes(dtype, bs):
     qf, kf, vf, bt, qs, kvs = host
     seg = lambda n: O.decode_segments(n, split=256, tile=64, warps=4)
     o_ks, l_ks, A = O.paged_attention_ref(qf, kf, vf, bt, qs, kvs, segments=seg, p_dtype=dtype,
-                                          with_tieband=True)
+                                          with_tieband=True, tieband_rule="rescaled")
     o = Hh.dev_to_f64(out)
     l = Hh.dev_to_f64(lse).reshape(o_ks.shape[:2])
     # the fp32 result (within A + 3e-6 of the oracle) is rounded to the input

@@ -72,7 +72,7 @@ void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens
     const int64_t group = p->num_heads / p->kv_heads;
     const int64_t mtiles = std::max<int64_t>(p->batch, ceil_div(p->num_tokens * group, 128));
     const int64_t units = p->kv_heads * mtiles;
-    const int64_t want = ceil_div(2 * kNumSMs, units);
+    const int64_t want = ceil_div(kNumSMs, units);  // one 225 KB CTA per SM
     int64_t ns = std::min<int64_t>(std::max<int64_t>(want, 1), ceil_div(cap, kTcTile));
     *split_tokens = ceil_div(ceil_div(cap, ns), kTcTile) * kTcTile;
   }

@@ -1,9 +1,308 @@
-// gate_up GEMM + SwiGLU epilogue (placeholder until the tcgen05 kernel lands).
+// gate_up GEMM with the SwiGLU epilogue fused, on tcgen05/TMEM.
+//
+//   C = X W^T,  X [M, K] bf16, W [2I, K] bf16 (nn.Linear layout: gate rows
+//   [0, I), up rows [I, 2I)); mode 1 writes D = silu(C_gate) * C_up in bf16
+//   ([M, I]) and never materialises C -- the fusion the reference only hooked
+//   (ascend-kernel/csrc/ops/f3_floor/op_kernel/kernel_f3_floor.cpp:276-282,
+//   intended chain f3_floor/design.md:107-109). Modes 0/2/4 also write C.
+//
+// Persistent kernel, one CTA per SM, 6 warps:
+//   warp 0    TMA producer: per 64-wide K block, the X tile [128 x 64] and the
+//             paired W tile = gate rows [n0, n0+BN) followed by up rows
+//             [I+n0, I+n0+BN) ([2BN x 64]), 128-byte swizzle, 4-stage ring;
+//   warp 1    MMA issuer: one tcgen05.mma M=128, N=2*BN, K=16 per K step, so
+//             a single TMEM accumulator holds gate (columns [0,BN)) and up
+//             (columns [BN,2BN)) of the same output tile; two accumulators
+//             (2 x 2BN = 512 columns) let the epilogue of tile t overlap the
+//             MMAs of tile t+1;
+//   warps 2-5 epilogue: thread = output row = TMEM lane; tcgen05.ld gate and
+//             up columns, silu(g) * u in fp32, RNE to bf16, swizzled smem
+//             staging, TMA tensor store (rows past M are clipped by TMA).
+// Tiles are visited m-fastest so the CTAs in flight share W tiles in L2 and
+// X stays L2-resident. No TMA multicast: every CTA loads its own tiles.
 #include "kernels.h"
+#include "ptx.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
 
 namespace cascade {
-cudaError_t launch_gateup(const GateUpLaunch&, const void*, const void*, cudaStream_t) { return cudaErrorNotSupported; }
-cudaError_t launch_gateup_window(const void*, void*, int64_t, int32_t, int32_t, int32_t, cudaStream_t) {
-  return cudaErrorNotSupported;
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 6 * 32;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kABytes = kBM * kBK * 2;          // 16 KB
+  static constexpr int kBBytes = 2 * BN * kBK * 2;       // 32 KB for BN=128
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStageOff = 0;
+  static constexpr int kStagingOff = kStages * kStageBytes;   // [128 rows x BN] bf16, SW128 halves
+  static constexpr int kStagingBytes = kBM * BN * 2;
+  static constexpr int kBarOff = kStagingOff + kStagingBytes;
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr uint32_t kTmemCols = 4 * BN;           // 2 accumulators x 2BN columns
+};
+
+struct __align__(8) GemmBars {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+struct GemmParams {
+  CUtensorMap tm_a;   // X [M, K], box {64, 128}
+  CUtensorMap tm_b;   // W [2I, K], box {64, BN}
+  CUtensorMap tm_d;   // D [M, I] row stride d_stride, box {64, 128}
+  CUtensorMap tm_c;   // C [M, 2I], box {64, 128}
+  int32_t M, K, I;
+  int32_t num_m, num_n, num_kb;
+  int32_t mode;
+};
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  // silu(g) = g / (1 + exp(-g)), exp via ex2; 1/(1+e) with an IEEE reciprocal
+  const float e = ex2(-g * 1.4426950408889634f);
+  return g * __frcp_rn(1.f + e) * u;
 }
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_constant__ GemmParams p) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  GemmBars* bars = reinterpret_cast<GemmBars*>(smem + C::kBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m * p.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 4 * 32);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile % p.num_m) * kBM;
+        const int n0 = (tile / p.num_m) * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int st = it % kStages;
+          if (it >= kStages) mbar_wait(&bars->empty[st], ((it / kStages) - 1) & 1);
+          uint8_t* sa = smem + C::kStageOff + st * C::kStageBytes;
+          uint8_t* sb = sa + C::kABytes;
+          mbar_arrive_expect_tx(&bars->full[st], C::kStageBytes);
+          tma_load_2d(sa, &p.tm_a, &bars->full[st], kb * kBK, m0);
+          tma_load_2d(sb, &p.tm_b, &bars->full[st], kb * kBK, n0);
+          tma_load_2d(sb + BN * 128, &p.tm_b, &bars->full[st], kb * kBK, p.I + n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(128, 2 * BN, 1, 0, 0);
+      const uint32_t sbase = smem_u32(smem + C::kStageOff);
+      int it = 0, tc = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
+        const int ab = tc & 1;
+        if (tc >= 2) mbar_wait(&bars->acc_empty[ab], ((tc >> 1) - 1) & 1);
+        tc_fence_after();
+        const uint32_t acc = tbase + ab * 2 * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int st = it % kStages;
+          mbar_wait(&bars->full[st], (it / kStages) & 1);
+          tc_fence_after();
+          const uint32_t a0 = sbase + st * C::kStageBytes;
+          const uint32_t b0 = a0 + C::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_f16_ss(acc, make_smem_desc(a0 + k * 32, 16, 1024, 2), make_smem_desc(b0 + k * 32, 16, 1024, 2),
+                        idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&bars->empty[st]);
+        }
+        umma_commit(&bars->acc_full[ab]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;            // tile row == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int etid = threadIdx.x - 64;      // 0..127 within the epilogue group
+    uint8_t* stg = smem + C::kStagingOff;
+    int tc = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
+      const int m0 = (tile % p.num_m) * kBM;
+      const int n0 = (tile / p.num_m) * BN;
+      const int ab = tc & 1;
+      mbar_wait(&bars->acc_full[ab], (tc >> 1) & 1);
+      tc_fence_after();
+      const uint32_t acc = tbase + lane_off + ab * 2 * BN;
+      // passes: mode 1 -> {silu*up -> D}; mode 2 -> {gate -> C, up -> C};
+      // mode 0 -> {gate -> C, up -> C, gate -> D}; mode 4 -> {gate -> C, up -> C, up -> D}
+      const int npass = p.mode == 1 ? 1 : (p.mode == 2 ? 2 : 3);
+      for (int pass = 0; pass < npass; ++pass) {
+        // the staging buffer must be free: previous bulk stores finished reading it
+        if (etid == 0) bulk_wait_group_read0();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int what = p.mode == 1 ? 2 : (pass < 2 ? pass : (p.mode == 0 ? 0 : 1));  // 0 gate, 1 up, 2 swiglu
+#pragma unroll
+        for (int c = 0; c < BN / 16; ++c) {
+          uint32_t g[16], u[16];
+          if (what != 1) tmem_ld_32x32b_x16(acc + c * 16, g);
+          if (what != 0) tmem_ld_32x32b_x16(acc + BN + c * 16, u);
+          tmem_wait_ld();
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            float a0, a1;
+            if (what == 2) {
+              a0 = silu_mul(__uint_as_float(g[e]), __uint_as_float(u[e]));
+              a1 = silu_mul(__uint_as_float(g[e + 1]), __uint_as_float(u[e + 1]));
+            } else if (what == 0) {
+              a0 = __uint_as_float(g[e]);
+              a1 = __uint_as_float(g[e + 1]);
+            } else {
+              a0 = __uint_as_float(u[e]);
+              a1 = __uint_as_float(u[e + 1]);
+            }
+            pk[e >> 1] = pack2<false>(a0, a1);
+          }
+          // column chunk (16 bytes = 8 outputs) index within the BN-wide tile
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int ch = c * 2 + h;
+            *reinterpret_cast<uint4*>(stg + (ch >> 3) * (kBM * 128) + sw128(r, ch & 7)) =
+                make_uint4(pk[4 * h], pk[4 * h + 1], pk[4 * h + 2], pk[4 * h + 3]);
+          }
+        }
+        if (pass == npass - 1) {
+          // all TMEM reads of this accumulator are done: hand it back
+          tc_fence_before();
+          mbar_arrive(&bars->acc_empty[ab]);
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (etid == 0) {
+          const bool to_d = (p.mode == 1) || pass == 2;
+#pragma unroll
+          for (int h = 0; h < BN / 64; ++h) {
+            if (to_d) {
+              tma_store_2d(&p.tm_d, stg + h * (kBM * 128), n0 + h * 64, m0);
+            } else {
+              const int col = (pass == 0 ? 0 : p.I) + n0 + h * 64;
+              tma_store_2d(&p.tm_c, stg + h * (kBM * 128), col, m0);
+            }
+          }
+          bulk_commit_group();
+        }
+      }
+    }
+    if (etid == 0) bulk_wait_group0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::kTmemCols);
+  }
+}
+
+// Modes 3/5/7/8: the epilogue's window traffic on an existing workspace.
+__global__ void gateup_window_kernel(const uint16_t* __restrict__ ws, uint16_t* __restrict__ d, int64_t d_stride,
+                                     int32_t M, int32_t I, int32_t mode) {
+  const int64_t chunks = static_cast<int64_t>(M) * (I / 8);
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < chunks;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = c / (I / 8), col = (c % (I / 8)) * 8;
+    if (mode == 7) {
+      // read-only rung: volatile loads of both windows, nothing written
+      const volatile uint4* gp = reinterpret_cast<const volatile uint4*>(ws + row * 2 * I + col);
+      const volatile uint4* up = reinterpret_cast<const volatile uint4*>(ws + row * 2 * I + I + col);
+      (void)gp->x;
+      (void)up->x;
+      continue;
+    }
+    uint4 g = make_uint4(0, 0, 0, 0);
+    if (mode != 8) g = *reinterpret_cast<const uint4*>(ws + row * 2 * I + col);
+    *reinterpret_cast<uint4*>(d + row * d_stride + col) = g;
+  }
+}
+
+bool enc(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t stride_bytes, uint32_t box_rows) {
+  return encode_tmap_2d(m, base, inner, rows, stride_bytes, 64, box_rows, true, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+}
+
+template <int BN>
+cudaError_t launch_bn(const GateUpLaunch& L, const void* a, const void* b, cudaStream_t stream) {
+  using C = GemmCfg<BN>;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = L.M;
+  p.K = L.K;
+  p.I = L.I;
+  p.num_m = (L.M + kBM - 1) / kBM;
+  p.num_n = L.I / BN;
+  p.num_kb = (L.K + kBK - 1) / kBK;
+  p.mode = L.mode;
+  if (!enc(&p.tm_a, a, L.K, L.M, static_cast<uint64_t>(L.K) * 2, kBM)) return cudaErrorInvalidValue;
+  if (!enc(&p.tm_b, b, L.K, 2ull * L.I, static_cast<uint64_t>(L.K) * 2, BN)) return cudaErrorInvalidValue;
+  if (L.mode != 2) {
+    if (!enc(&p.tm_d, L.d, L.I, L.M, static_cast<uint64_t>(L.d_stride) * 2, kBM)) return cudaErrorInvalidValue;
+  }
+  if (L.mode != 1) {
+    if (!enc(&p.tm_c, L.ws, 2ull * L.I, L.M, 4ull * L.I, kBM)) return cudaErrorInvalidValue;
+  }
+  int dev = 0, sms = kNumSMs;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = p.num_m * p.num_n;
+  const int grid = tiles < sms ? tiles : sms;
+  cudaError_t e = cudaFuncSetAttribute(gateup_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  gateup_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gateup(const GateUpLaunch& L, const void* a, const void* b, cudaStream_t stream) {
+  return launch_bn<128>(L, a, b, stream);
+}
+
+cudaError_t launch_gateup_window(const void* ws, void* d, int64_t d_stride, int32_t M, int32_t I, int32_t mode,
+                                 cudaStream_t stream) {
+  const int64_t chunks = static_cast<int64_t>(M) * (I / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((chunks + 255) / 256, 148 * 16));
+  gateup_window_kernel<<<blocks, 256, 0, stream>>>(static_cast<const uint16_t*>(ws), static_cast<uint16_t*>(d),
+                                                   d_stride, M, I, mode);
+  return cudaGetLastError();
+}
+
 }  // namespace cascade

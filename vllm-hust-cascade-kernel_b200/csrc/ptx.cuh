@@ -113,6 +113,25 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
+// 2-D tiled store smem -> global (bulk-group completion). Rows/columns of
+// the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* desc, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Wait until all committed bulk stores of this thread have finished READING smem.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Wait until all committed bulk stores of this thread are complete.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor core / TMA reads of smem written by threads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
