@@ -127,6 +127,23 @@ CASCADE_API int cascade_lse_merge(const void *o1, int32_t o1_dtype, const void *
 CASCADE_API int cascade_f3_gateup_epilogue(const void *a, const void *b, void *ws, void *d, int64_t d_stride, int64_t M,
                                int64_t K, int64_t I, int32_t mode, cascade_stream_t stream);
 
+/* Suffix decode that allocates nothing (no counterpart in the reference).
+ * For callers that cannot allocate device memory when they run the step: a
+ * host binding the C ABI without a device allocator, or a serving loop whose
+ * memory is fixed before it starts. Same inputs, outputs and results as
+ * cascade_suffix_decode, but the split-KV partials go to a scratch array
+ * built into the library: 16 MiB, reserved on every GPU that loads the
+ * library until the process exits. Limits: q_seqlen_value must be > 0, and a
+ * call whose cascade_suffix_decode_workspace_size() exceeds 16 MiB is
+ * rejected with CASCADE_ERR_UNSUPPORTED before anything runs. The first call
+ * on each device looks up the array's device address (cudaGetSymbolAddress
+ * with that device current); make that first call before any stream capture.
+ * All calls share the one array and nothing in it needs clearing (each call
+ * writes every partial it reads), but calls that overlap on the GPU (other
+ * streams, other host threads) race on it: serialise them. */
+CASCADE_API int cascade_suffix_decode_noalloc(const cascade_paged_attn_t *p, void *out, float *lse,
+                                              cascade_stream_t stream);
+
 /* Last error message of this thread ("" if none). */
 CASCADE_API const char *cascade_last_error(void);
 

@@ -18,6 +18,7 @@ EXPORTED = [
     "cascade_fa_fp32_stage1",
     "cascade_suffix_decode_workspace_size",
     "cascade_suffix_decode",
+    "cascade_suffix_decode_noalloc",
     "cascade_lse_merge",
     "cascade_f3_gateup_epilogue",
     "cascade_last_error",
@@ -79,6 +80,8 @@ def load():
     lib.cascade_fa_fp32_stage1.restype = ctypes.c_int
     lib.cascade_suffix_decode.argtypes = [P, vp, vp, vp, sz, vp]
     lib.cascade_suffix_decode.restype = ctypes.c_int
+    lib.cascade_suffix_decode_noalloc.argtypes = [P, vp, vp, vp]
+    lib.cascade_suffix_decode_noalloc.restype = ctypes.c_int
     lib.cascade_lse_merge.argtypes = [vp, i32, vp, i32, vp, i64, vp, i64, vp, i32, i64, i64, vp]
     lib.cascade_lse_merge.restype = ctypes.c_int
     lib.cascade_f3_gateup_epilogue.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
@@ -175,6 +178,12 @@ def suffix_decode(desc, out, lse, workspace=None, stream=None):
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     return check(lib.cascade_suffix_decode(ctypes.byref(desc), _ptr(out), _ptr(lse), _ptr(workspace),
                                            ws_bytes, stream_ptr(stream)))
+
+
+def suffix_decode_noalloc(desc, out, lse, stream=None):
+    """The allocation-free suffix decode (fixed 16 MiB scratch inside the library)."""
+    return check(load().cascade_suffix_decode_noalloc(ctypes.byref(desc), _ptr(out), _ptr(lse),
+                                                      stream_ptr(stream)))
 
 
 def stage1_workspace_size(desc):

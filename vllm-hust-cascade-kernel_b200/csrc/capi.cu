@@ -233,6 +233,11 @@ bool encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   return r == CUDA_SUCCESS;
 }
 
+int set_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+
 }  // namespace cascade
 
 using namespace cascade;

@@ -75,6 +75,9 @@ cudaError_t launch_gateup(const GateUpLaunch& p, const void* a, const void* b, c
 cudaError_t launch_gateup_window(const void* ws, void* d, int64_t d_stride, int32_t M, int32_t I, int32_t mode,
                                  cudaStream_t stream);
 
+// Host: record `msg` as this thread's cascade_last_error() text; returns `code`.
+int set_error(int code, const char* msg);
+
 // Host: encode a 2-D bf16/fp16 tiled tensor map (SW128 when inner box is 64).
 bool encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
                     uint32_t box_inner, uint32_t box_rows, bool swizzle128, CUtensorMapL2promotion promo);
