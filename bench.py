@@ -148,19 +148,18 @@ def run_ours(args, rank, world, local):
     def step():
         return cascade_decode(w.q, w.k_pool, w.v_pool, t)
 
-    def suffix_op():
-        return npu.cascade_suffix_decode(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens,
-                                         t.suffix_kv_seqlens, 1)
+    # the dominant kernel alone: the suffix decode kernel writing its split
+    # partials (C ABI, CASCADE_FLAG_PARTIALS_ONLY: one launch, no combine)
+    dom_desc = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens,
+                               t.suffix_kv_seqlens, 1, flags=capi.FLAG_PARTIALS_ONLY)
+    dom_ws = torch.empty(capi.suffix_workspace_size(dom_desc), dtype=torch.uint8, device="cuda")
 
-    # launches per step (the planner tells how many split-combine kernels run)
+    def suffix_op():
+        capi.suffix_decode(dom_desc, None, None, dom_ws)
+
+    # one step = stage-1 kernel + suffix decode kernel + the step combine
     def n_launches():
-        d1 = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.prefix_block_table, t.prefix_q_seqlens,
-                             t.prefix_kv_seqlens, t.uniform_group)
-        d2 = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens,
-                             t.suffix_kv_seqlens, 1)
-        p1 = capi.plan(d1, t.uniform_group, False)
-        p2 = capi.plan(d2, 1, True)
-        return (1 + (p1.num_splits > 1)) + (1 + (p2.num_splits > 1)) + 1
+        return 3
 
     for _ in range(args.warmup):
         step()
@@ -187,22 +186,29 @@ def run_ours(args, rank, world, local):
     step_ms = max_over_ranks(step_ms, world)
     dom_ms = max_over_ranks(dom_ms, world)
 
-    # e2e through the public op with host buffers
-    q_h = w.q.cpu().pin_memory()
+    # e2e through the public op with host buffers: every step copies its inputs
+    # (q and the six index tensors, packed into one pinned host buffer -> one
+    # H2D copy) and reads the merged output back (one D2H copy)
     tabs = [t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens, t.suffix_block_table,
             t.suffix_q_seqlens, t.suffix_kv_seqlens]
-    tabs_h = [x.cpu().pin_memory() for x in tabs]
+    parts = [w.q] + tabs
+    offs, cur = [], 0
+    for x in parts:
+        offs.append(cur)
+        cur += (x.numel() * x.element_size() + 255) // 256 * 256
+    host_in = torch.empty(cur, dtype=torch.uint8).pin_memory()
+    for x, o in zip(parts, offs):
+        nb = x.numel() * x.element_size()
+        host_in[o:o + nb].copy_(x.contiguous().view(-1).view(torch.uint8).cpu())
+    dev_in = torch.empty(cur, dtype=torch.uint8, device="cuda")
+    views = [dev_in[o:o + x.numel() * x.element_size()].view(x.dtype).view(x.shape) for x, o in zip(parts, offs)]
     out_h = torch.empty(w.q.shape, dtype=torch.bfloat16).pin_memory()
-    q_d = torch.empty_like(w.q)
-    tabs_d = [torch.empty_like(x) for x in tabs]
     from cascade_kernel.cascade import CascadeTables
+    tt = CascadeTables(*views[1:], uniform_group=t.uniform_group)
 
     def e2e_step():
-        q_d.copy_(q_h, non_blocking=True)
-        for d_, h_ in zip(tabs_d, tabs_h):
-            d_.copy_(h_, non_blocking=True)
-        tt = CascadeTables(*tabs_d, uniform_group=t.uniform_group)
-        out = cascade_decode(q_d, w.k_pool, w.v_pool, tt)
+        dev_in.copy_(host_in, non_blocking=True)
+        out = cascade_decode(views[0], w.k_pool, w.v_pool, tt)
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(max(3, args.warmup)):
@@ -217,13 +223,15 @@ def run_ours(args, rank, world, local):
         e2e_ev[i][1].record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_ev) / args.steps, world)
-    h2d = q_h.numel() * q_h.element_size() + sum(x.numel() * x.element_size() for x in tabs_h)
+    h2d = cur
     d2h = out_h.numel() * out_h.element_size()
 
     total_bytes = ab["total"] * world
     value = total_bytes / (step_ms * 1e-3) / 1e9
     dom_bytes = ab["suffix"]
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+
+    gateup = gateup_sweep(flush, peaks) if not args.no_gateup else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -252,7 +260,7 @@ def run_ours(args, rank, world, local):
             "l2": "flushed (256 MiB write) before every timed step",
         },
         "roofline": {
-            "kernel": "suffix decode op (paged_decode_kernel + split_combine_kernel)",
+            "kernel": "paged_decode_kernel (suffix decode, split partials; one launch)",
             "bound": "hbm",
             "achieved": round(achieved, 1),
             "peak": peaks["hbm_gbs"],
@@ -264,13 +272,50 @@ def run_ours(args, rank, world, local):
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "us_per_step": round(e2e_ms * 1e3, 2), "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
-        "gpu_launches": n_launches() * args.steps + 2 * args.steps,
+        "gpu_launches": n_launches() * args.steps + args.steps,
         "clocks": clk.summary(),
     }
     line["frac_of_hbm_roofline_step"] = round(value / world / peaks["hbm_gbs"], 4)
+    if gateup is not None:
+        line["gateup_swiglu"] = gateup
+        line["gpu_launches"] += gateup.pop("_launches")
     if cpu is not None:
         line["cpu_baseline"] = cpu
     return line
+
+
+def gateup_sweep(flush, peaks, Ms=(1, 16, 64, 256, 4096), K=4096, I=14336, reps=5):
+    """Llama-3-8B gate_up + SwiGLU: X[M,4096] x W[2*14336,4096]^T -> bf16 [M,14336]
+    through torch.ops.npu.cascade_gateup_swiglu (one tcgen05 kernel per call).
+    Per M: TFLOP/s (tensor bound at M=4096) and GB/s (HBM bound for M<=256)."""
+    import torch
+    npu = torch.ops.npu
+    g = torch.Generator(device="cuda").manual_seed(7)
+    w = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    res, launches = {}, 0
+    for M in Ms:
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        for _ in range(3):
+            npu.cascade_gateup_swiglu(x, w)
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            npu.cascade_gateup_swiglu(x, w)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+            launches += 1
+        ts.sort()
+        us = ts[len(ts) // 2]
+        flops = 2.0 * M * K * 2 * I
+        byts = 2.0 * M * K + 2.0 * 2 * I * K + 2.0 * M * I
+        res[str(M)] = {"us": round(us, 2), "tflops": round(flops / us / 1e6, 1), "gbs": round(byts / us / 1e3, 1),
+                       "frac_tensor": round(flops / us / 1e6 / peaks["bf16_tflops"], 4),
+                       "frac_hbm": round(byts / us / 1e3 / peaks["hbm_gbs"], 4)}
+    return {"shape": "X[M,4096] x W[28672,4096]^T -> silu(gate)*up bf16 [M,14336]", "per_M": res,
+            "peak_tflops": peaks["bf16_tflops"], "peak_src": peaks["src"], "_launches": launches}
 
 
 # ----------------------------------------------------------------- CPU baseline
@@ -356,6 +401,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gateup", action="store_true", help="skip the gate_up SwiGLU sweep")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -74,6 +74,11 @@ typedef struct cascade_paged_attn {
   int32_t flags; /* reserved, pass 0 */
 } cascade_paged_attn_t;
 
+/* cascade_paged_attn_t.flags bit: write the split-KV partials
+ * (workspace layout below) and skip the final combine; out/lse are not
+ * touched. Used to time or chain the attention kernel alone. */
+#define CASCADE_FLAG_PARTIALS_ONLY 1
+
 /* Bytes of device workspace a call with this description needs (split-KV
  * partials). Depends on shapes only, never on the seqlen values. 0 = none. */
 CASCADE_API size_t cascade_fa_fp32_stage1_workspace_size(const cascade_paged_attn_t *p);
@@ -99,6 +104,24 @@ CASCADE_API int cascade_fa_fp32_stage1(const cascade_paged_attn_t *p, float *out
 CASCADE_API size_t cascade_suffix_decode_workspace_size(const cascade_paged_attn_t *p);
 CASCADE_API int cascade_suffix_decode(const cascade_paged_attn_t *p, void *out, float *lse, void *workspace,
                           size_t workspace_bytes, cascade_stream_t stream);
+
+/* One whole cascade decode step (stage-1 over the shared prefixes, the
+ * per-request suffixes, and the merge) with a single final combine: both
+ * attention kernels write split partials into the workspace and one kernel
+ * merges all partials of each (token, head) row in LSE space and writes
+ * `out` ([num_tokens, num_heads, 128] in out_dtype) and, if lse_out is not
+ * NULL, the merged natural-log LSE ([num_tokens*num_heads] fp32).
+ * Equivalent to cascade_fa_fp32_stage1 + cascade_suffix_decode +
+ * cascade_lse_merge (the consumer's chain, ascend-kernel/README.md:158-201)
+ * without the intermediate outputs; the suffix partial is not rounded to the
+ * query dtype before the merge. `prefix` and `suffix` describe the same
+ * query tensor (same num_tokens / num_heads / dtype); zero-length prefixes or
+ * suffixes are allowed. */
+CASCADE_API size_t cascade_decode_step_workspace_size(const cascade_paged_attn_t *prefix,
+                                                      const cascade_paged_attn_t *suffix);
+CASCADE_API int cascade_decode_step(const cascade_paged_attn_t *prefix, const cascade_paged_attn_t *suffix, void *out,
+                                    int32_t out_dtype, float *lse_out, void *workspace, size_t workspace_bytes,
+                                    cascade_stream_t stream);
 
 /* Row-wise LSE-space merge of two attention partials.
  * Replaces ascend_kernel::lse_merge

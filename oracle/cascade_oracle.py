@@ -349,14 +349,16 @@ def gateup_ref_fp64(x, w):
 # ---------------------------------------------------------------------------
 
 def cascade_step_ref(q, k, v, prefix_bt, group_sizes, prefix_lens, suffix_bt, suffix_lens, *,
-                     p_dtype="bf16", out_dtype="bf16", kv_heads_subset=None):
+                     p_dtype="bf16", out_dtype="bf16", kv_heads_subset=None, round_suffix=True):
     """fp64 cascade step.  q [B,H,D]; k/v [NB,bs,KVH,D] (grid values);
     prefix_bt [G,cols]; suffix_bt [B,cols].  Stage-1 flattens each prefix
     group's requests into one request of q_len = group size (README.md:174-177);
     the suffix runs per request with q_len 1; the merge follows
     lse_merge_cases.py:45-50.  ``kv_heads_subset`` restricts the computation
-    to those kv heads (and their query heads).  Returns (out [B,H',D] rounded
-    to out_dtype, lse [B,H'])."""
+    to those kv heads (and their query heads).  ``round_suffix=False`` keeps
+    the suffix partial unrounded (the single-combine step does not round it
+    to the query dtype before merging).  Returns (out [B,H',D] rounded to
+    out_dtype, lse [B,H'])."""
     q = np.asarray(q, np.float64)
     B, H, D = q.shape
     KVH = k.shape[2]
@@ -370,6 +372,7 @@ def cascade_step_ref(q, k, v, prefix_bt, group_sizes, prefix_lens, suffix_bt, su
                                  p_dtype=p_dtype)
     o2, l2 = paged_attention_ref(q, k, v, suffix_bt, np.ones(B, np.int64), np.asarray(suffix_lens),
                                  p_dtype=p_dtype)
-    o2 = quantize(o2, p_dtype)          # the suffix output is in the input dtype
+    if round_suffix:
+        o2 = quantize(o2, p_dtype)      # the suffix output is in the input dtype
     out, lse = lse_merge_ref(o1, o2, l1, l2)
     return quantize(out, out_dtype), lse

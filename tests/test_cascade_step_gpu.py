@@ -1,0 +1,126 @@
+"""GPU parity of the whole cascade decode step: the fused single-combine op
+(npu.cascade_decode_step / C ABI cascade_decode_step) and the reference
+consumer's three-op chain, against the CPU oracle of the composed step
+(oracle.cascade_step_ref) and against each other at the benchmark shape."""
+import numpy as np
+import pytest
+
+import helpers as Hh
+from oracle import cascade_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _work(name, **kw):
+    from cascade_kernel import workloads
+    return workloads.make_cascade(name, device="cuda", **kw)
+
+
+CASES = {
+    # C1-like: 4 requests share a 512-token prefix, fp16, H=8/KVH=2
+    "c1_like": dict(group_sizes=[4], prefix_lens=[512], suffix_lens=[64, 100, 200, 256], H=8, KVH=2, bs=128,
+                    dtype="fp16", seed=1),
+    # C2-like at reduced batch (the oracle must finish in seconds): bf16, 32/8 heads
+    "c2_like_b16": dict(group_sizes=[16], prefix_lens=[1024], suffix_lens=list(range(128, 1024, 56)), H=32,
+                        KVH=8, bs=128, dtype="bf16", seed=2),
+    # ragged: several prefix groups, block size 16, zero-length suffixes, GQA 5
+    "ragged_bs16": dict(group_sizes=[3, 3, 3], prefix_lens=[16, 300, 777], suffix_lens=[0, 5, 200, 0, 31, 64, 1, 0, 90],
+                        H=10, KVH=2, bs=16, dtype="fp16", seed=3),
+    # many rows per kv head: 40 requests x group 5 -> 200 rows (two 128-row tiles)
+    "wide_group": dict(group_sizes=[40], prefix_lens=[640], suffix_lens=[7] * 40, H=10, KVH=2, bs=64,
+                       dtype="bf16", seed=4),
+}
+
+
+def _oracle(w, round_suffix, out_dtype):
+    f64 = lambda x: x.float().cpu().numpy().astype(np.float64)
+    p_dtype = "bf16" if str(w.q.dtype) == "torch.bfloat16" else "fp16"
+    return O.cascade_step_ref(f64(w.q), f64(w.k_pool), f64(w.v_pool), w.tables.prefix_block_table.cpu().numpy(),
+                              w.group_sizes, w.prefix_lens, w.tables.suffix_block_table.cpu().numpy(),
+                              w.suffix_lens, p_dtype=p_dtype, out_dtype=out_dtype, round_suffix=round_suffix)
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_fused_step_and_chain_vs_oracle(name):
+    import torch
+    from cascade_kernel.cascade import cascade_decode
+    Hh.need_cuda()
+    kw = dict(CASES[name])
+    kw["dtype"] = torch.float16 if kw["dtype"] == "fp16" else torch.bfloat16
+    w = _work(name, **kw)
+    dt = "fp16" if kw["dtype"] == torch.float16 else "bf16"
+    fused = cascade_decode(w.q, w.k_pool, w.v_pool, w.tables, fused=True)
+    chain = cascade_decode(w.q, w.k_pool, w.v_pool, w.tables, fused=False)
+    torch.cuda.synchronize()
+    assert Hh.capi().device_error() == 0
+    ref_f, _ = _oracle(w, round_suffix=False, out_dtype="fp32")
+    ref_c, _ = _oracle(w, round_suffix=True, out_dtype="fp32")
+    got_f, got_c = Hh.dev_to_f64(fused), Hh.dev_to_f64(chain)
+    assert np.isfinite(got_f).all() and np.isfinite(got_c).all()
+    # BASELINE bar
+    np.testing.assert_allclose(got_f, ref_f, atol=2e-2, rtol=2e-2)
+    np.testing.assert_allclose(got_c, ref_c, atol=2e-2, rtol=2e-2)
+    # tighter: one output ulp plus the P-rounding structure difference of the
+    # attention kernels against the 512-chunk golden structure
+    for got, ref in ((got_f, ref_f), (got_c, ref_c)):
+        err = np.abs(got - ref)
+        assert (err <= O.ulp(ref, dt) + 2e-3).all(), float((err - O.ulp(ref, dt)).max())
+
+
+def test_fused_equals_chain_at_benchmark_shape():
+    """C2 (B=64, prefix 4096, suffix U[128,1024], 32/8 heads): the fused step and
+    the three-op chain differ only by the chain's rounding of the suffix
+    partial to bf16 before the merge: within one bf16 ulp everywhere."""
+    import torch
+    from cascade_kernel import workloads
+    from cascade_kernel.cascade import cascade_decode
+    Hh.need_cuda()
+    w = workloads.c2_llama8b(seed=0)
+    t = w.tables
+    fused = cascade_decode(w.q, w.k_pool, w.v_pool, t, fused=True)
+    chain = cascade_decode(w.q, w.k_pool, w.v_pool, t, fused=False)
+    o2, _ = torch.ops.npu.cascade_suffix_decode(w.q, w.k_pool, w.v_pool, t.suffix_block_table,
+                                                t.suffix_q_seqlens, t.suffix_kv_seqlens, 1)
+    torch.cuda.synchronize()
+    a, b = Hh.dev_to_f64(fused), Hh.dev_to_f64(chain)
+    # each side rounds once to bf16 (<= 1 ulp apart) and the chain also rounds
+    # the suffix partial (weight <= 1) before merging (<= half an ulp of o2)
+    bound = O.ulp(np.maximum(np.abs(a), np.abs(b)), "bf16") + 0.5 * O.ulp(Hh.dev_to_f64(o2), "bf16") + 1e-7
+    excess = np.abs(a - b) - bound
+    assert (excess <= 0).all(), float(excess.max())
+
+
+def test_decode_step_capi_and_partials_only_flag():
+    import torch
+    from cascade_kernel import workloads
+    Hh.need_cuda()
+    C = Hh.capi()
+    npu = Hh.ops()
+    w = workloads.c1_cpu_golden(seed=3)
+    t = w.tables
+    dp = C.paged_desc(w.q, w.k_pool, w.v_pool, t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens,
+                      t.uniform_group)
+    ds = C.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens, t.suffix_kv_seqlens, 1)
+    n = C.decode_step_workspace_size(dp, ds)
+    ws = torch.empty(max(n, 1), dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(w.q)
+    lse = torch.empty(w.q.shape[0] * w.q.shape[1], dtype=torch.float32, device="cuda")
+    C.decode_step(dp, ds, out, lse, ws)
+    ref = npu.cascade_decode_step(w.q, w.k_pool, w.v_pool, t.prefix_block_table, t.prefix_q_seqlens,
+                                  t.prefix_kv_seqlens, t.suffix_block_table, t.suffix_q_seqlens,
+                                  t.suffix_kv_seqlens, t.uniform_group, 3)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    _, l_ref = _oracle(w, round_suffix=False, out_dtype="fp16")
+    assert np.abs(Hh.dev_to_f64(lse).reshape(l_ref.shape) - l_ref).max() < 1e-3
+    # partials-only: the suffix kernel alone, no combine, out untouched
+    dpo = C.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens, t.suffix_kv_seqlens, 1,
+                       flags=C.FLAG_PARTIALS_ONLY)
+    m = C.suffix_workspace_size(dpo)
+    assert m > 0
+    ws2 = torch.empty(m, dtype=torch.uint8, device="cuda")
+    o2 = torch.full_like(w.q, 5.0)
+    l2 = torch.empty_like(lse)
+    C.suffix_decode(dpo, o2, l2, ws2)
+    torch.cuda.synchronize()
+    assert torch.all(o2 == 5.0)

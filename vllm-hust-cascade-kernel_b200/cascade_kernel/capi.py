@@ -19,6 +19,8 @@ EXPORTED = [
     "cascade_suffix_decode_workspace_size",
     "cascade_suffix_decode",
     "cascade_suffix_decode_noalloc",
+    "cascade_decode_step_workspace_size",
+    "cascade_decode_step",
     "cascade_lse_merge",
     "cascade_f3_gateup_epilogue",
     "cascade_last_error",
@@ -82,6 +84,10 @@ def load():
     lib.cascade_suffix_decode.restype = ctypes.c_int
     lib.cascade_suffix_decode_noalloc.argtypes = [P, vp, vp, vp]
     lib.cascade_suffix_decode_noalloc.restype = ctypes.c_int
+    lib.cascade_decode_step_workspace_size.argtypes = [P, P]
+    lib.cascade_decode_step_workspace_size.restype = sz
+    lib.cascade_decode_step.argtypes = [P, P, vp, i32, vp, vp, sz, vp]
+    lib.cascade_decode_step.restype = ctypes.c_int
     lib.cascade_lse_merge.argtypes = [vp, i32, vp, i32, vp, i64, vp, i64, vp, i32, i64, i64, vp]
     lib.cascade_lse_merge.restype = ctypes.c_int
     lib.cascade_f3_gateup_epilogue.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
@@ -129,8 +135,11 @@ def dtype_code(torch_dtype):
     return {torch.bfloat16: BF16, torch.float16: FP16, torch.float32: FP32}[torch_dtype]
 
 
+FLAG_PARTIALS_ONLY = 1
+
+
 def paged_desc(query, key, value, block_table, q_seqlens, kv_seqlens, q_seqlen_value=0, *,
-               shape=None, dtype=None):
+               shape=None, dtype=None, flags=0):
     """Build the C descriptor from device tensors (or from explicit shapes when
     ``shape`` = dict of sizes is given and the tensors are None)."""
     d = PagedAttn()
@@ -148,7 +157,7 @@ def paged_desc(query, key, value, block_table, q_seqlens, kv_seqlens, q_seqlen_v
             setattr(d, k, v)
         d.dtype = BF16 if dtype is None else dtype
     d.q_seqlen_value = q_seqlen_value
-    d.flags = 0
+    d.flags = flags
     return d
 
 
@@ -184,6 +193,18 @@ def suffix_decode_noalloc(desc, out, lse, stream=None):
     """The allocation-free suffix decode (fixed 16 MiB scratch inside the library)."""
     return check(load().cascade_suffix_decode_noalloc(ctypes.byref(desc), _ptr(out), _ptr(lse),
                                                       stream_ptr(stream)))
+
+
+def decode_step(prefix, suffix, out, lse_out=None, workspace=None, stream=None):
+    """cascade_decode_step through the C ABI (out in its own dtype)."""
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    return check(load().cascade_decode_step(ctypes.byref(prefix), ctypes.byref(suffix), _ptr(out),
+                                            dtype_code(out.dtype), _ptr(lse_out), _ptr(workspace), ws_bytes,
+                                            stream_ptr(stream)))
+
+
+def decode_step_workspace_size(prefix, suffix):
+    return load().cascade_decode_step_workspace_size(ctypes.byref(prefix), ctypes.byref(suffix))
 
 
 def stage1_workspace_size(desc):

@@ -35,15 +35,25 @@ class CascadeTables:
     uniform_group: int = 0
 
 
-def cascade_decode(q, k_pool, v_pool, tables: CascadeTables, out_dtype=None):
+def cascade_decode(q, k_pool, v_pool, tables: CascadeTables, out_dtype=None, fused=True):
     """One cascade decode step for one layer.
 
     q [B, H, 128] (bf16 or fp16), k_pool/v_pool [numBlocks, bs, KVH, 128].
     Returns the merged attention output [B, H, 128] in ``out_dtype``
-    (default: the query dtype).  bf16 + block size 128 uses exactly the
-    reference ops (fa_fp32_stage1 / lse_merge out_code=1); other inputs use
-    the extended-domain siblings."""
+    (default: the query dtype).
+
+    fused=True (default): ``npu.cascade_decode_step`` -- stage-1 and suffix
+    kernels write split partials and one combine kernel writes the output.
+    fused=False: the reference consumer's chain of three ops; bf16 + block
+    size 128 uses exactly the reference ops (fa_fp32_stage1 / lse_merge
+    out_code=1), other inputs the extended-domain siblings."""
     out_dtype = q.dtype if out_dtype is None else out_dtype
+    code = {torch.bfloat16: 1, torch.float32: 2, torch.float16: 3}[out_dtype]
+    if fused:
+        return torch.ops.npu.cascade_decode_step(
+            q, k_pool, v_pool, tables.prefix_block_table, tables.prefix_q_seqlens, tables.prefix_kv_seqlens,
+            tables.suffix_block_table, tables.suffix_q_seqlens, tables.suffix_kv_seqlens, tables.uniform_group,
+            code)
     reference_domain = (q.dtype == torch.bfloat16 and k_pool.shape[1] == 128
                         and out_dtype == torch.bfloat16)
     npu = torch.ops.npu
@@ -52,7 +62,6 @@ def cascade_decode(q, k_pool, v_pool, tables: CascadeTables, out_dtype=None):
                     tables.prefix_kv_seqlens, tables.uniform_group)
     o2, l2 = npu.cascade_suffix_decode(q, k_pool, v_pool, tables.suffix_block_table,
                                        tables.suffix_q_seqlens, tables.suffix_kv_seqlens, 1)
-    code = {torch.bfloat16: 1, torch.float32: 2, torch.float16: 3}[out_dtype]
     if reference_domain:
         return npu.lse_merge(o1, o2, l1, l2, code)
     return npu.cascade_lse_merge(o1, o2, l1, l2, code)

@@ -60,6 +60,7 @@ bool block_size_ok(int64_t bs) {
 
 constexpr int kDecodeSplit = 256;  // kv tokens per decode split (multiple of its 64-token tile)
 constexpr int kTcTile = 128;       // kv tokens per tcgen05 tile
+constexpr int kMaxSplits = 32;     // per request; the step combine merges up to 64 partials per row
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -67,20 +68,21 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens, int64_t* num_splits) {
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
   if (kernel == 0) {
-    *split_tokens = kDecodeSplit;
+    // 256-token splits, widened (in 64-token tiles) so no request has more than kMaxSplits
+    *split_tokens = std::max<int64_t>(kDecodeSplit, ceil_div(ceil_div(cap, kMaxSplits), 64) * 64);
   } else {
     const int64_t group = p->num_heads / p->kv_heads;
     const int64_t mtiles = std::max<int64_t>(p->batch, ceil_div(p->num_tokens * group, 128));
     const int64_t units = p->kv_heads * mtiles;
     const int64_t want = ceil_div(kNumSMs, units);  // one 225 KB CTA per SM
-    int64_t ns = std::min<int64_t>(std::max<int64_t>(want, 1), ceil_div(cap, kTcTile));
+    int64_t ns = std::min<int64_t>(std::min<int64_t>(std::max<int64_t>(want, 1), ceil_div(cap, kTcTile)), kMaxSplits);
     *split_tokens = ceil_div(ceil_div(cap, ns), kTcTile) * kTcTile;
   }
   *num_splits = ceil_div(cap, *split_tokens);
 }
 
 size_t workspace_for(const cascade_paged_attn_t* p, int64_t num_splits) {
-  if (num_splits <= 1) return 0;
+  if (num_splits <= 1 && !(p->flags & CASCADE_FLAG_PARTIALS_ONLY)) return 0;
   const size_t rows = static_cast<size_t>(p->num_tokens) * p->num_heads;
   return static_cast<size_t>(num_splits) * rows * (kHeadDim + 1) * sizeof(float);
 }
@@ -150,68 +152,93 @@ int read_and_check_seqlens(const cascade_paged_attn_t* p, const char* op, bool a
   return CASCADE_OK;
 }
 
-int run_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, void* out, float* lse, void* ws,
-              size_t ws_bytes, cudaStream_t stream) {
+// Validation, seqlen read-back (legacy path), planning and tensor maps of one
+// paged-attention call. On success *L holds everything but the output and
+// workspace pointers. Returns CASCADE_OK with plan->num_splits == 0 for an
+// empty problem (nothing to launch).
+int prepare_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, cudaStream_t stream,
+                  cascade_attn_plan_t* plan, PagedAttnLaunch* L) {
   int rc = validate_paged(p, op);
   if (rc == CASCADE_OK) rc = validate_pointers(p, op);
   if (rc) return rc;
-  if (p->batch == 0 || p->num_tokens == 0) return CASCADE_OK;
-  if (!out || !lse) return fail(CASCADE_ERR_INVALID, "%s: null output pointer", op);
+  std::memset(L, 0, sizeof(*L));
+  if (p->batch == 0 || p->num_tokens == 0) {
+    plan->num_splits = 0;
+    return CASCADE_OK;
+  }
   int64_t max_q = p->q_seqlen_value;
   if (p->q_seqlen_value == 0) {
     rc = read_and_check_seqlens(p, op, suffix, stream, &max_q);
     if (rc) return rc;
   }
-  cascade_attn_plan_t plan;
-  rc = cascade_plan_paged_attn(p, max_q, suffix ? 1 : 0, &plan);
+  rc = cascade_plan_paged_attn(p, max_q, suffix ? 1 : 0, plan);
   if (rc) return rc;
-  if (plan.num_splits > 1) {
-    if (ws == nullptr || ws_bytes < plan.workspace_bytes)
-      return fail(CASCADE_ERR_WORKSPACE, "%s: workspace of %zu bytes required, %zu given", op,
-                  plan.workspace_bytes, ws_bytes);
-    if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(CASCADE_ERR_INVALID, "%s: workspace must be 16-byte aligned", op);
-  }
-
-  PagedAttnLaunch L;
-  std::memset(&L, 0, sizeof(L));
-  const bool tc = plan.kernel == 1;
+  const bool tc = plan->kernel == 1;
   const uint32_t box_rows = static_cast<uint32_t>(std::min<int64_t>(p->block_size, tc ? 128 : 64));
   const uint64_t inner = static_cast<uint64_t>(p->kv_heads) * kHeadDim;
   const uint64_t rows = static_cast<uint64_t>(p->num_blocks) * p->block_size;
   if (rows == 0) return fail(CASCADE_ERR_INVALID, "%s: empty KV pool", op);
-  if (!encode_tmap_2d(&L.tmap_k, p->key, inner, rows, inner * 2, 64, box_rows, true,
+  if (!encode_tmap_2d(&L->tmap_k, p->key, inner, rows, inner * 2, 64, box_rows, true,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
-      !encode_tmap_2d(&L.tmap_v, p->value, inner, rows, inner * 2, 64, box_rows, true,
+      !encode_tmap_2d(&L->tmap_v, p->value, inner, rows, inner * 2, 64, box_rows, true,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
     return fail(CASCADE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed", op);
-  L.query = p->query;
-  L.block_table = p->block_table;
-  L.q_seqlens = p->actual_q_seqlens;
-  L.kv_seqlens = p->actual_kv_seqlens;
+  L->query = p->query;
+  L->block_table = p->block_table;
+  L->q_seqlens = p->actual_q_seqlens;
+  L->kv_seqlens = p->actual_kv_seqlens;
+  L->num_tokens = static_cast<int32_t>(p->num_tokens);
+  L->num_heads = static_cast<int32_t>(p->num_heads);
+  L->kv_heads = static_cast<int32_t>(p->kv_heads);
+  L->group = static_cast<int32_t>(p->num_heads / p->kv_heads);
+  L->batch = static_cast<int32_t>(p->batch);
+  L->block_cols = static_cast<int32_t>(p->block_cols);
+  L->block_size = static_cast<int32_t>(p->block_size);
+  L->num_blocks = static_cast<int32_t>(p->num_blocks);
+  L->q_seqlen_value = static_cast<int32_t>(p->q_seqlen_value);
+  L->max_q_seqlen = static_cast<int32_t>(max_q);
+  L->split_tokens = static_cast<int32_t>(plan->split_tokens);
+  L->num_splits = static_cast<int32_t>(plan->num_splits);
+  L->out_dtype = suffix ? p->dtype : CASCADE_FP32;
+  L->lse_stride = suffix ? 1 : 8;
+  L->partial_out = (p->flags & CASCADE_FLAG_PARTIALS_ONLY) ? 1 : 0;
+  L->scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(kHeadDim)) * 1.4426950408889634);
+  return CASCADE_OK;
+}
+
+int check_workspace(const char* op, void* ws, size_t ws_bytes, size_t need) {
+  if (need == 0) return CASCADE_OK;
+  if (ws == nullptr || ws_bytes < need)
+    return fail(CASCADE_ERR_WORKSPACE, "%s: workspace of %zu bytes required, %zu given", op, need, ws_bytes);
+  if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(CASCADE_ERR_INVALID, "%s: workspace must be 16-byte aligned", op);
+  return CASCADE_OK;
+}
+
+void set_partials(PagedAttnLaunch* L, void* ws) {
+  const size_t nrows = static_cast<size_t>(L->num_tokens) * L->num_heads;
+  L->part_o = static_cast<float*>(ws);
+  L->part_lse = ws ? static_cast<float*>(ws) + static_cast<size_t>(L->num_splits) * nrows * kHeadDim : nullptr;
+}
+
+cudaError_t launch_attention(const PagedAttnLaunch& L, int kernel, bool fp16, cudaStream_t stream) {
+  return kernel == 1 ? launch_paged_prefix_tc(L, fp16, stream) : launch_paged_decode(L, fp16, stream);
+}
+
+int run_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, void* out, float* lse, void* ws,
+              size_t ws_bytes, cudaStream_t stream) {
+  cascade_attn_plan_t plan;
+  PagedAttnLaunch L;
+  int rc = prepare_paged(p, op, suffix, stream, &plan, &L);
+  if (rc || plan.num_splits == 0) return rc;
+  const bool partials_only = L.partial_out != 0;
+  if (!partials_only && (!out || !lse)) return fail(CASCADE_ERR_INVALID, "%s: null output pointer", op);
+  rc = check_workspace(op, ws, ws_bytes, plan.workspace_bytes);
+  if (rc) return rc;
   L.out = out;
   L.lse = lse;
-  const size_t nrows = static_cast<size_t>(p->num_tokens) * p->num_heads;
-  L.part_o = static_cast<float*>(ws);
-  L.part_lse = ws ? static_cast<float*>(ws) + static_cast<size_t>(plan.num_splits) * nrows * kHeadDim : nullptr;
-  L.num_tokens = static_cast<int32_t>(p->num_tokens);
-  L.num_heads = static_cast<int32_t>(p->num_heads);
-  L.kv_heads = static_cast<int32_t>(p->kv_heads);
-  L.group = static_cast<int32_t>(p->num_heads / p->kv_heads);
-  L.batch = static_cast<int32_t>(p->batch);
-  L.block_cols = static_cast<int32_t>(p->block_cols);
-  L.block_size = static_cast<int32_t>(p->block_size);
-  L.num_blocks = static_cast<int32_t>(p->num_blocks);
-  L.q_seqlen_value = static_cast<int32_t>(p->q_seqlen_value);
-  L.max_q_seqlen = static_cast<int32_t>(max_q);
-  L.split_tokens = static_cast<int32_t>(plan.split_tokens);
-  L.num_splits = static_cast<int32_t>(plan.num_splits);
-  L.out_dtype = suffix ? p->dtype : CASCADE_FP32;
-  L.lse_stride = suffix ? 1 : 8;
-  L.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(kHeadDim)) * 1.4426950408889634);
-
-  const bool fp16 = p->dtype == CASCADE_FP16;
-  cudaError_t e = tc ? launch_paged_prefix_tc(L, fp16, stream) : launch_paged_decode(L, fp16, stream);
-  if (e == cudaSuccess && plan.num_splits > 1) e = launch_split_combine(L, stream);
+  set_partials(&L, ws);
+  cudaError_t e = launch_attention(L, plan.kernel, p->dtype == CASCADE_FP16, stream);
+  if (e == cudaSuccess && plan.num_splits > 1 && !partials_only) e = launch_split_combine(L, stream);
   if (e != cudaSuccess) return cuda_fail(op, e);
   return CASCADE_OK;
 }
@@ -306,6 +333,68 @@ int cascade_suffix_decode(const cascade_paged_attn_t* p, void* out, float* lse, 
                           size_t workspace_bytes, cascade_stream_t stream) {
   return run_paged(p, "cascade_suffix_decode", true, out, lse, workspace, workspace_bytes,
                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+size_t cascade_decode_step_workspace_size(const cascade_paged_attn_t* prefix, const cascade_paged_attn_t* suffix) {
+  if (!prefix || !suffix) return 0;
+  cascade_paged_attn_t a = *prefix, b = *suffix;
+  a.flags |= CASCADE_FLAG_PARTIALS_ONLY;
+  b.flags |= CASCADE_FLAG_PARTIALS_ONLY;
+  return align_up(workspace_size_any(&a, 1), 256) + align_up(workspace_size_any(&b, 1), 256);
+}
+
+int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_attn_t* suffix, void* out,
+                        int32_t out_dtype, float* lse_out, void* workspace, size_t workspace_bytes,
+                        cascade_stream_t stream) {
+  const char* op = "cascade_decode_step";
+  if (!prefix || !suffix) return fail(CASCADE_ERR_INVALID, "%s: null argument", op);
+  if (out_dtype != CASCADE_BF16 && out_dtype != CASCADE_FP16 && out_dtype != CASCADE_FP32)
+    return fail(CASCADE_ERR_INVALID, "%s: out dtype must be bf16, fp16 or fp32", op);
+  if (prefix->num_tokens != suffix->num_tokens || prefix->num_heads != suffix->num_heads ||
+      prefix->dtype != suffix->dtype || prefix->head_dim != suffix->head_dim)
+    return fail(CASCADE_ERR_INVALID, "%s: prefix and suffix must describe the same query tensor", op);
+  const size_t rows = static_cast<size_t>(suffix->num_tokens) * suffix->num_heads;
+  if (rows == 0) return CASCADE_OK;
+  if (!out) return fail(CASCADE_ERR_INVALID, "%s: null output pointer", op);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cascade_paged_attn_t a = *prefix, b = *suffix;
+  a.flags |= CASCADE_FLAG_PARTIALS_ONLY;
+  b.flags |= CASCADE_FLAG_PARTIALS_ONLY;
+  cascade_attn_plan_t pa, pb;
+  PagedAttnLaunch La, Lb;
+  int rc = prepare_paged(&a, op, true, st, &pa, &La);
+  if (rc == CASCADE_OK) rc = prepare_paged(&b, op, true, st, &pb, &Lb);
+  if (rc) return rc;
+  const size_t need_a = pa.num_splits ? align_up(pa.workspace_bytes, 256) : 0;
+  const size_t need_b = pb.num_splits ? align_up(pb.workspace_bytes, 256) : 0;
+  rc = check_workspace(op, workspace, workspace_bytes, need_a + need_b);
+  if (rc) return rc;
+  set_partials(&La, workspace);
+  set_partials(&Lb, static_cast<uint8_t*>(workspace) + need_a);
+  const bool fp16 = suffix->dtype == CASCADE_FP16;
+  if ((pa.num_splits ? La.num_splits : 0) + (pb.num_splits ? Lb.num_splits : 0) > 64)
+    return fail(CASCADE_ERR_UNSUPPORTED, "%s: more than 64 KV splits per row", op);
+  cudaError_t e = cudaSuccess;
+  if (pa.num_splits) e = launch_attention(La, pa.kernel, fp16, st);
+  if (e == cudaSuccess && pb.num_splits) e = launch_attention(Lb, pb.kernel, fp16, st);
+  if (e == cudaSuccess) {
+    CascadeCombineLaunch C;
+    C.o1 = La.part_o;
+    C.l1 = La.part_lse;
+    C.n1 = pa.num_splits ? La.num_splits : 0;
+    C.o2 = Lb.part_o;
+    C.l2 = Lb.part_lse;
+    C.n2 = pb.num_splits ? Lb.num_splits : 0;
+    C.rows = static_cast<int64_t>(rows);
+    C.out = out;
+    C.out_dtype = out_dtype;
+    C.lse_out = lse_out;
+    e = launch_cascade_combine(C, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(op, e);
+  return CASCADE_OK;
 }
 
 int cascade_lse_merge(const void* o1, int32_t o1_dtype, const void* o2, int32_t o2_dtype, const float* lse1,

@@ -31,6 +31,7 @@ struct PagedAttnLaunch {
   int32_t split_tokens, num_splits;
   int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
   int32_t lse_stride;   // 8 (reference padded rows) or 1 (compact)
+  int32_t partial_out;  // 1: always write split partials (a later combine produces the output)
   float scale_log2;     // softmax scale * log2(e)
 };
 
@@ -41,6 +42,22 @@ cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStre
 
 // Merge the nsplit partials of every (token, head) row into the final output.
 cudaError_t launch_split_combine(const PagedAttnLaunch& p, cudaStream_t stream);
+
+// One combine for a whole cascade step: merges the split partials of stage-1
+// and of the suffix for every (token, head) row and writes the final output.
+struct CascadeCombineLaunch {
+  const float* o1;      // [n1][rows][128]
+  const float* l1;      // [n1][rows]
+  const float* o2;      // [n2][rows][128]
+  const float* l2;      // [n2][rows]
+  int32_t n1, n2;
+  int64_t rows;
+  void* out;            // [rows][128] in out_dtype
+  int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
+  float* lse_out;       // [rows] or null
+};
+
+cudaError_t launch_cascade_combine(const CascadeCombineLaunch& p, cudaStream_t stream);
 
 // ----------------------------------------------------------------------------
 // LSE merge

@@ -32,11 +32,14 @@ constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kHalfBytes = kTile * 128;          // one [64 tokens x 64 dims] 16-bit box region
 constexpr int kKBytes = 2 * kHalfBytes;           // K tile, both dim halves
 constexpr int kStageBytes = 2 * kKBytes;          // K + V
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 512 /*barriers, block-table cache*/;
+
+constexpr int kBtCache = 48;  // block-table entries of one split kept in smem
 
 struct __align__(8) DecodeBarriers {
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  int32_t bt[kBtCache];
 };
 
 __device__ __forceinline__ int request_token_offset(const PagedAttnLaunch& p, int b) {
@@ -84,7 +87,7 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
   // Empty split (kv shorter than this split's start, or no query rows):
   // write -inf partials so the combine step skips it.
   if (ntiles == 0 || nrows == 0) {
-    if (p.num_splits > 1) {
+    if (p.num_splits > 1 || p.partial_out) {
       for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
         int t = tok0 + r / p.group, h = g * p.group + r % p.group;
         p.part_lse[static_cast<size_t>(split) * p.num_tokens * p.num_heads + static_cast<size_t>(t) * p.num_heads + h] =
@@ -117,14 +120,25 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
+    // The whole warp first pulls this split's block-table entries into shared
+    // memory, so the TMA issue loop never waits on a dependent global load.
+    const int bs = p.block_size;
+    const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
+    const int npages = (kv + bs - 1) / bs;
+    const int first_page = s_begin / bs;
+    const int last_page = min(npages, (s_end + bs - 1) / bs);  // exclusive
+    const int nbt = last_page - first_page;
+    const bool cached = nbt <= kBtCache;
+    if (cached) {
+      for (int i = lane; i < nbt; i += 32) bars->bt[i] = bt[first_page + i];
+    }
+    __syncwarp();
     if (lane == 0) {
       tma_prefetch_desc(&p.tmap_k);
       tma_prefetch_desc(&p.tmap_v);
-      const int bs = p.block_size;
       const int box_rows = bs < kTile ? bs : kTile;
       const int oob_row = p.num_blocks * bs;  // fully out of range -> zero fill
-      const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
-      const int npages = (kv + bs - 1) / bs;
+      const uint64_t pol = policy_evict_first();
       for (int i = 0; i < ntiles; ++i) {
         const int st = i % kStages;
         if (i >= kStages) mbar_wait(&bars->empty[st], ((i / kStages) - 1) & 1);
@@ -135,19 +149,15 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
         for (int off = 0; off < kTile; off += box_rows) {
           const int t = t_tile + off;
           const int page = t / bs;
-          int row;
-          if (page < npages) {
-            row = bt[page] * bs + (t % bs);
-          } else {
-            row = oob_row;
-          }
+          int row = oob_row;
+          if (page < npages) row = (cached ? bars->bt[page - first_page] : bt[page]) * bs + (t % bs);
           const int x0 = g * kHeadDim;
           uint8_t* dk = sk + off * 128;
           uint8_t* dv = sv + off * 128;
-          tma_load_2d(dk, &p.tmap_k, &bars->full[st], x0, row);
-          tma_load_2d(dk + kHalfBytes, &p.tmap_k, &bars->full[st], x0 + 64, row);
-          tma_load_2d(dv, &p.tmap_v, &bars->full[st], x0, row);
-          tma_load_2d(dv + kHalfBytes, &p.tmap_v, &bars->full[st], x0 + 64, row);
+          tma_load_2d_hint(dk, &p.tmap_k, &bars->full[st], x0, row, pol);
+          tma_load_2d_hint(dk + kHalfBytes, &p.tmap_k, &bars->full[st], x0 + 64, row, pol);
+          tma_load_2d_hint(dv, &p.tmap_v, &bars->full[st], x0, row, pol);
+          tma_load_2d_hint(dv + kHalfBytes, &p.tmap_v, &bars->full[st], x0 + 64, row, pol);
         }
       }
     }
@@ -350,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
         acc[j + 3] += wt[w] * v.w;
       }
     }
-    if (p.num_splits > 1) {
+    if (p.num_splits > 1 || p.partial_out) {
       float* dst = p.part_o + (static_cast<size_t>(split) * p.num_tokens * p.num_heads + row) * kHeadDim + d0;
 #pragma unroll
       for (int j = 0; j < 16; j += 4)

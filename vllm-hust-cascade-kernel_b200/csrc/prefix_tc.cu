@@ -7,24 +7,26 @@
 // QK^T / PV contraction (the shared-prefix stage of the reference,
 // ascend-kernel/csrc/ops/fa_fp32_stage1/op_kernel/kernel_fa_fp32_stage1.cpp:143-745).
 //
-// One CTA = (KV split, kv head x 128-row tile, request); 6 warps:
-//   warp 4    TMA producer: 128-token K and V tiles, gathered page by page
-//             through block_table (2-D boxes of [min(bs,128) rows x 64 dims],
+// One CTA = (KV split, kv head x 128-row tile, request); 10 warps:
+//   warp 8    TMA producer: 128-token K and V tiles gathered page by page
+//             through block_table (2-D boxes [min(bs,128) rows x 64 dims],
 //             128-byte swizzle), double-buffered;
-//   warp 5    MMA issuer (one thread): S = Q K^T (M=128, N=128, K=128) into a
-//             TMEM S buffer, then O_tile = P V into a TMEM PV buffer; every
-//             completion is signalled with tcgen05.commit to an mbarrier;
-//   warps 0-3 softmax + correction: thread i owns query row i == TMEM lane i.
-//             Reads S with tcgen05.ld, keeps the running max / row sum, writes
-//             P = bf16/fp16(exp(S - m)) (RNE, the reference's quantisation
-//             point, block_epilogue_online_softmax_no_mask.hpp:578-591) into
-//             swizzled smem as the A operand of PV, and accumulates
-//             O = dm * O + PV in registers (the reference's rescale,
-//             block_epilogue_rescale_o_no_split_row.hpp:144-268).
-// TMEM: S[2] at columns 0/128, PV[2] at 256/384 (512 columns, 1 CTA per SM).
-// Shared memory: Q 32 KB, K 2x32 KB, V 2x32 KB, P 2x32 KB.
-// Final O/l and LSE = ln(l) + m (natural log), written 8x per row (stage-1
-// padded layout) or as a split partial merged by the combine kernel.
+//   warp 9    MMA issuer (one thread): S_j = Q K_j^T (M=N=K=128) into a TMEM S
+//             buffer; O += P_j V_j into the TMEM O accumulator;
+//   warps 0-3 softmax: thread i owns query row i == TMEM lane i. One
+//             tcgen05.ld of the 128-column S row, running max and
+//             unquantised row sum, P = round16(exp(S - m)) (RNE: the
+//             reference's quantisation point,
+//             block_epilogue_online_softmax_no_mask.hpp:578-591) into swizzled
+//             smem as the A operand of PV;
+//   warps 4-7 correction + epilogue: before P_j V_j is accumulated, the TMEM
+//             accumulator is rescaled O = dm_j * O (the reference's rescale,
+//             block_epilogue_rescale_o_no_split_row.hpp:144-268) -- skipped,
+//             exactly, for a warp whose 32 rows all kept their max (dm == 1);
+//             they also load Q and write the final O / l and LSE.
+// TMEM: S[2] at columns 0/128, O at 256. Shared memory: Q 32 KB, K 2x32 KB,
+// V 2x32 KB, P 32 KB. LSE = ln(l) + m (natural log), written 8x per row
+// (stage-1 padded layout) or as a split partial for a later combine.
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -33,21 +35,27 @@ namespace {
 
 constexpr int kRows = 128;
 constexpr int kTok = 128;
-constexpr int kThreads = 6 * 32;
+constexpr int kThreads = 10 * 32;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr int kHalf = 16384;            // [128 rows][64 x 16-bit] swizzled region
 constexpr int kTileBytes = 2 * kHalf;   // [128 rows][128 x 16-bit]
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTileBytes;
 constexpr int kOffV = kOffK + 2 * kTileBytes;
 constexpr int kOffP = kOffV + 2 * kTileBytes;
-constexpr int kOffBar = kOffP + 2 * kTileBytes;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;
+constexpr int kOffAux = kOffP + kTileBytes;   // dm[2][128], l[128], m[128], barriers
+constexpr int kSmemBytes = kOffAux + 4 * 128 * 4 + 256 + 1024;
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;
 
 struct __align__(8) PrefixBars {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_free[2], p_full[2], p_free[2], pv_full[2], pv_free[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full, p_free;
+  uint64_t stat_full[2], o_ready[2];
+  uint64_t o_final, fin;
   uint32_t tmem_base;
 };
 
@@ -61,21 +69,38 @@ __device__ __forceinline__ int token_offset(const PagedAttnLaunch& p, int b) {
   return static_cast<int>(acc);
 }
 
-__device__ __forceinline__ void store_row(const PagedAttnLaunch& p, size_t row, const float* o, float scale) {
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Stores 32 consecutive output elements of one row (fp32 or 16-bit).
+__device__ __forceinline__ void store_chunk(const PagedAttnLaunch& p, size_t elem, const uint32_t (&r)[32],
+                                            float scale) {
   if (p.out_dtype == 2) {
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * kHeadDim);
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + elem);
 #pragma unroll
-    for (int i = 0; i < kHeadDim / 4; ++i)
-      dst[i] = make_float4(o[4 * i] * scale, o[4 * i + 1] * scale, o[4 * i + 2] * scale, o[4 * i + 3] * scale);
+    for (int i = 0; i < 8; ++i)
+      dst[i] = make_float4(__uint_as_float(r[4 * i]) * scale, __uint_as_float(r[4 * i + 1]) * scale,
+                           __uint_as_float(r[4 * i + 2]) * scale, __uint_as_float(r[4 * i + 3]) * scale);
   } else {
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + row * kHeadDim);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + elem);
     const bool h = p.out_dtype == 1;
 #pragma unroll
-    for (int i = 0; i < kHeadDim / 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
       uint32_t w[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float a = o[8 * i + 2 * j] * scale, b = o[8 * i + 2 * j + 1] * scale;
+        const float a = __uint_as_float(r[8 * i + 2 * j]) * scale, b = __uint_as_float(r[8 * i + 2 * j + 1]) * scale;
         w[j] = h ? pack2<true>(a, b) : pack2<false>(a, b);
       }
       dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -87,7 +112,10 @@ template <bool kFp16>
 __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __grid_constant__ PagedAttnLaunch p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  PrefixBars* bars = reinterpret_cast<PrefixBars*>(smem + kOffBar);
+  float* dmbuf = reinterpret_cast<float*>(smem + kOffAux);   // [2][128]
+  float* lbuf = dmbuf + 2 * kRows;                            // [128]
+  float* mbuf = lbuf + kRows;                                 // [128]
+  PrefixBars* bars = reinterpret_cast<PrefixBars*>(mbuf + kRows);
 
   const int split = blockIdx.x;
   const int g = blockIdx.y % p.kv_heads;
@@ -108,6 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
   const int s_end = min(kv, s_begin + p.split_tokens);
   const int ntiles = s_end > s_begin ? (s_end - s_begin + kTok - 1) / kTok : 0;
   const size_t plane = static_cast<size_t>(p.num_tokens) * p.num_heads;
+  const bool partial = p.num_splits > 1 || p.partial_out;
 
   auto out_row = [&](int r) -> size_t {
     const int rr = row0 + r;
@@ -118,13 +147,14 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
     // split beyond this request's kv (or kv == 0)
     for (int r = tid; r < unit_rows; r += blockDim.x) {
       const size_t row = out_row(r);
-      if (p.num_splits > 1) {
+      if (partial) {
         p.part_lse[static_cast<size_t>(split) * plane + row] = -INFINITY;
       } else {
-        float z[kHeadDim];
+        uint32_t z[32];
 #pragma unroll
-        for (int i = 0; i < kHeadDim; ++i) z[i] = 0.f;
-        store_row(p, row, z, 1.f);
+        for (int i = 0; i < 32; ++i) z[i] = 0u;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) store_chunk(p, row * kHeadDim + c * 32, z, 1.f);
         for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = -INFINITY;
       }
     }
@@ -139,15 +169,17 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_free[s], 4 * 32);
-      mbar_init(&bars->p_full[s], 4 * 32);
-      mbar_init(&bars->p_free[s], 1);
-      mbar_init(&bars->pv_full[s], 1);
-      mbar_init(&bars->pv_free[s], 4 * 32);
+      mbar_init(&bars->s_free[s], 128);
+      mbar_init(&bars->stat_full[s], 128);
+      mbar_init(&bars->o_ready[s], 128);
     }
+    mbar_init(&bars->p_full, 128);
+    mbar_init(&bars->p_free, 1);
+    mbar_init(&bars->o_final, 1);
+    mbar_init(&bars->fin, 128);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -155,12 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
-  const uint32_t sQ = smem_u32(smem + kOffQ);
-  const uint32_t sK = smem_u32(smem + kOffK);
-  const uint32_t sV = smem_u32(smem + kOffV);
-  const uint32_t sP = smem_u32(smem + kOffP);
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&p.tmap_k);
@@ -191,12 +219,16 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = kFp16 ? 0u : 1u;
       const uint32_t idesc_s = make_idesc_f16(128, 128, fmt, 0, 0);
       const uint32_t idesc_pv = make_idesc_f16(128, 128, fmt, 0, 1);
+      const uint32_t sQ = smem_u32(smem + kOffQ);
+      const uint32_t sK = smem_u32(smem + kOffK);
+      const uint32_t sV = smem_u32(smem + kOffV);
+      const uint32_t sP = smem_u32(smem + kOffP);
       mbar_wait(&bars->q_full, 0);
       tc_fence_after();
       for (int j = 0; j <= ntiles; ++j) {
@@ -219,133 +251,161 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
           const int i = j - 1;
           const int st = i & 1, u = i >> 1;
           mbar_wait(&bars->v_full[st], u & 1);
-          mbar_wait(&bars->p_full[st], u & 1);
-          if (i >= 2) mbar_wait(&bars->pv_free[st], (u - 1) & 1);
+          mbar_wait(&bars->p_full, i & 1);
+          mbar_wait(&bars->o_ready[st], u & 1);
           tc_fence_after();
-          const uint32_t pb = sP + st * kTileBytes;
           const uint32_t vb = sV + st * kTileBytes;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            umma_f16_ss(tbase + 256 + st * 128,
-                        make_smem_desc(pb + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024, 2),
-                        make_smem_desc(vb + k * 2048, kHalf, 1024, 2), idesc_pv, k > 0 ? 1u : 0u);
+            umma_f16_ss(tbase + kColO, make_smem_desc(sP + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024, 2),
+                        make_smem_desc(vb + k * 2048, kHalf, 1024, 2), idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&bars->pv_full[st]);
           umma_commit(&bars->v_empty[st]);
-          umma_commit(&bars->p_free[st]);
+          umma_commit(&bars->p_free);
+          if (i == ntiles - 1) umma_commit(&bars->o_final);
         }
       }
     }
-  } else {
-    // ------------------------------------------------ softmax / correction
-    // Q row -> swizzled smem (K-major A operand); rows past the unit are zero
-    {
-      uint8_t* q_s = smem + kOffQ;
-      if (tid < unit_rows) {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.query) +
-                                                           out_row(tid) * kHeadDim);
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          *reinterpret_cast<uint4*>(q_s + (c >> 3) * kHalf + sw128(tid, c & 7)) = __ldg(src + c);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          *reinterpret_cast<uint4*>(q_s + (c >> 3) * kHalf + sw128(tid, c & 7)) = make_uint4(0, 0, 0, 0);
-      }
-      fence_proxy_async_smem();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid == 0) mbar_arrive(&bars->q_full);
-    }
-
+  } else if (warp < 4) {
+    // ---------------------------------------------------------------- softmax
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const float sl2 = p.scale_log2;
-    float o[kHeadDim];
-#pragma unroll
-    for (int i = 0; i < kHeadDim; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, dm_prev = 0.f;
-
-    auto accumulate = [&](int i, float d) {
-      const int st = i & 1, u = i >> 1;
-      mbar_wait(&bars->pv_full[st], u & 1);
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(tbase + lane_off + 256 + st * 128 + c * 16, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) o[c * 16 + e] = fmaf(d, o[c * 16 + e], __uint_as_float(r[e]));
-      }
-      tc_fence_before();
-      mbar_arrive(&bars->pv_free[st]);
-    };
-
+    uint8_t* pbuf = smem + kOffP;
+    float m = -INFINITY, l = 0.f;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1, u = j >> 1;
       const int n_valid = min(kTok, s_end - (s_begin + j * kTok));
       mbar_wait(&bars->s_full[st], u & 1);
       tc_fence_after();
-      const uint32_t s_addr = tbase + lane_off + st * 128;
+      uint32_t s0[32], s1[32], s2[32], s3[32];
+      tmem_ld_32x32b_x32(tbase + lane_off + st * 128 + 0, s0);
+      tmem_ld_32x32b_x32(tbase + lane_off + st * 128 + 32, s1);
+      tmem_ld_32x32b_x32(tbase + lane_off + st * 128 + 64, s2);
+      tmem_ld_32x32b_x32(tbase + lane_off + st * 128 + 96, s3);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars->s_free[st]);  // S is in registers: the buffer may be overwritten
+      float s[128];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        s[e] = __uint_as_float(s0[e]);
+        s[32 + e] = __uint_as_float(s1[e]);
+        s[64 + e] = __uint_as_float(s2[e]);
+        s[96 + e] = __uint_as_float(s3[e]);
+      }
+      if (n_valid < kTok) {
+#pragma unroll
+        for (int e = 0; e < kTok; ++e) s[e] = e < n_valid ? s[e] : -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(s_addr + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float v = (c * 32 + e < n_valid) ? __uint_as_float(r[e]) : -INFINITY;
-          mx = fmaxf(mx, v);
-        }
-      }
+      for (int e = 0; e < kTok; ++e) mx = fmaxf(mx, s[e]);
       const float m_new = fmaxf(m, mx * sl2);
-      const float dm = (m == -INFINITY) ? 0.f : ex2(m - m_new);
-      if (j >= 2) mbar_wait(&bars->p_free[st], (u - 1) & 1);
-      uint8_t* pbuf = smem + kOffP + st * kTileBytes;
+      const float dm = (m == -INFINITY) ? 1.f : ex2(m - m_new);
+      dmbuf[st * kRows + tid] = dm;
+      mbar_arrive(&bars->stat_full[st]);
       float rs = 0.f;
+      uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(s_addr + c * 16, r);
-        tmem_wait_ld();
-        uint32_t pk[8];
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          const float x0 = (c * 16 + e < n_valid) ? ex2(fmaf(__uint_as_float(r[e]), sl2, -m_new)) : 0.f;
-          const float x1 = (c * 16 + e + 1 < n_valid) ? ex2(fmaf(__uint_as_float(r[e + 1]), sl2, -m_new)) : 0.f;
-          rs += x0 + x1;
-          pk[e >> 1] = pack2<kFp16>(x0, x1);
-        }
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int tc = c * 2 + q;  // 16-byte chunk index along the 128 tokens
-          *reinterpret_cast<uint4*>(pbuf + (tc >> 3) * kHalf + sw128(tid, tc & 7)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        }
+      for (int e = 0; e < kTok; e += 2) {
+        const float x0 = ex2(fmaf(s[e], sl2, -m_new));      // masked: ex2(-inf) = 0
+        const float x1 = ex2(fmaf(s[e + 1], sl2, -m_new));
+        rs += x0 + x1;
+        pk[e >> 1] = pack2<kFp16>(x0, x1);
       }
-      tc_fence_before();
-      mbar_arrive(&bars->s_free[st]);
+      if (j >= 1) mbar_wait(&bars->p_free, (j - 1) & 1);  // PV_{j-1} finished reading P
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        *reinterpret_cast<uint4*>(pbuf + (c >> 3) * kHalf + sw128(tid, c & 7)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      }
       fence_proxy_async_smem();
-      mbar_arrive(&bars->p_full[st]);
+      mbar_arrive(&bars->p_full);
       l = dm * l + rs;
       m = m_new;
-      if (j >= 1) accumulate(j - 1, dm_prev);
-      dm_prev = dm;
     }
-    accumulate(ntiles - 1, dm_prev);
-
-    if (tid < unit_rows) {
-      const size_t row = out_row(tid);
-      const float inv = 1.f / l;
-      const float lse_nat = (m + __log2f(l)) * 0.6931471805599453f;
-      if (p.num_splits > 1) {
-        float4* dst = reinterpret_cast<float4*>(p.part_o + (static_cast<size_t>(split) * plane + row) * kHeadDim);
+    lbuf[tid] = l;
+    mbuf[tid] = m;
+    mbar_arrive(&bars->fin);
+  } else {
+    // -------------------------------------------- correction + epilogue (4-7)
+    const int r = tid - 128;  // row == TMEM lane (warp % 4 selects the lane quarter)
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    {
+      // Q row -> swizzled smem (K-major A operand); rows past the unit are zero
+      uint8_t* q_s = smem + kOffQ;
+      if (r < unit_rows) {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.query) +
+                                                           out_row(r) * kHeadDim);
+        uint4 v[16];
 #pragma unroll
-        for (int i = 0; i < kHeadDim / 4; ++i)
-          dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+        for (int c = 0; c < 16; ++c) v[c] = __ldg(src + c);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(q_s + (c >> 3) * kHalf + sw128(r, c & 7)) = v[c];
+      } else {
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          *reinterpret_cast<uint4*>(q_s + (c >> 3) * kHalf + sw128(r, c & 7)) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (r == 0) mbar_arrive(&bars->q_full);
+    }
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1, u = j >> 1;
+      mbar_wait(&bars->stat_full[st], u & 1);
+      const float dm = dmbuf[st * kRows + r];
+      if (j >= 1 && __any_sync(0xffffffffu, dm != 1.f)) {
+        // O must hold P_{j-1} V_{j-1} before it is rescaled. PV MMAs complete
+        // in order and PV_{j-2} is already complete here (the softmax waited
+        // for it before writing P_{j-1}), so the parity of p_free is unambiguous.
+        mbar_wait(&bars->p_free, (j - 1) & 1);
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tbase + lane_off + kColO + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * dm);
+          tmem_st_32x32b_x32(tbase + lane_off + kColO + c * 32, o);
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->o_ready[st]);
+    }
+    // epilogue: O / l once the last PV is done
+    mbar_wait(&bars->fin, 0);
+    mbar_wait(&bars->o_final, 0);
+    tc_fence_after();
+    const float l = lbuf[r], m = mbuf[r];
+    const float inv = 1.f / l;
+    const float lse_nat = (m + __log2f(l)) * 0.6931471805599453f;
+    const bool valid = r < unit_rows;
+    const size_t row = valid ? out_row(r) : 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      tmem_ld_32x32b_x32(tbase + lane_off + kColO + c * 32, o);
+      tmem_wait_ld();
+      if (valid) {
+        if (partial) {
+          float4* dst = reinterpret_cast<float4*>(p.part_o + (static_cast<size_t>(split) * plane + row) * kHeadDim +
+                                                  c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                 __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+        } else {
+          store_chunk(p, row * kHeadDim + c * 32, o, inv);
+        }
+      }
+    }
+    if (valid) {
+      if (partial) {
         p.part_lse[static_cast<size_t>(split) * plane + row] = lse_nat;
       } else {
-        store_row(p, row, o, inv);
         for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = lse_nat;
       }
     }
@@ -353,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
   }

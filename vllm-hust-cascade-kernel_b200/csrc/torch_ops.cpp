@@ -160,6 +160,32 @@ std::tuple<at::Tensor, at::Tensor> cascade_suffix_decode(const at::Tensor& query
   return {out, lse};
 }
 
+// torch.ops.npu.cascade_decode_step -- the whole cascade step with one final
+// combine (C ABI cascade_decode_step). Returns the merged output [T,H,D] in
+// the dtype selected by out_code (1 bf16, 2 fp32, 3 fp16).
+at::Tensor cascade_decode_step(const at::Tensor& query, const at::Tensor& key, const at::Tensor& value,
+                               const at::Tensor& prefix_block_table, const at::Tensor& prefix_q_seqlens,
+                               const at::Tensor& prefix_kv_seqlens, const at::Tensor& suffix_block_table,
+                               const at::Tensor& suffix_q_seqlens, const at::Tensor& suffix_kv_seqlens,
+                               int64_t prefix_q_seqlen_value, int64_t out_code) {
+  const char* op = "cascade_decode_step";
+  TORCH_CHECK(out_code >= 1 && out_code <= 3, op, ": out_code must be 1 (bf16), 2 (fp32) or 3 (fp16)");
+  cascade_paged_attn_t a = paged_desc(op, false, query, key, value, prefix_block_table, prefix_q_seqlens,
+                                      prefix_kv_seqlens, prefix_q_seqlen_value);
+  cascade_paged_attn_t b = paged_desc(op, false, query, key, value, suffix_block_table, suffix_q_seqlens,
+                                      suffix_kv_seqlens, 1);
+  const c10::cuda::CUDAGuard guard(query.device());
+  const at::ScalarType out_type = out_code == 1 ? at::kBFloat16 : out_code == 2 ? at::kFloat : at::kHalf;
+  auto out = at::empty(query.sizes(), query.options().dtype(out_type));
+  if (query.numel() == 0) return out;
+  const size_t ws_bytes = cascade_decode_step_workspace_size(&a, &b);
+  at::Tensor ws;
+  if (ws_bytes) ws = at::empty({static_cast<int64_t>(ws_bytes)}, query.options().dtype(at::kByte));
+  check_rc(cascade_decode_step(&a, &b, out.data_ptr(), dtype_code(out_type), nullptr,
+                               ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, current_stream(query)));
+  return out;
+}
+
 at::Tensor merge_impl(const char* op, bool strict, const at::Tensor& o1, const at::Tensor& o2, const at::Tensor& lse1,
                       const at::Tensor& lse2, int64_t out_code) {
   // op_host/lse_merge.cpp:35-60, same order and texts
@@ -301,6 +327,10 @@ TORCH_LIBRARY_FRAGMENT(npu, m) {
       "Tensor actual_q_seqlens, Tensor actual_kv_seqlens, int q_seqlen_value=0) -> (Tensor, Tensor)");
   m.def("cascade_lse_merge(Tensor o1, Tensor o2, Tensor lse1, Tensor lse2, int out_code=0) -> Tensor");
   m.def("cascade_gateup_swiglu(Tensor x, Tensor w) -> Tensor");
+  m.def(
+      "cascade_decode_step(Tensor query, Tensor key, Tensor value, Tensor prefix_block_table, "
+      "Tensor prefix_q_seqlens, Tensor prefix_kv_seqlens, Tensor suffix_block_table, Tensor suffix_q_seqlens, "
+      "Tensor suffix_kv_seqlens, int prefix_q_seqlen_value=0, int out_code=1) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(npu, CUDA, m) {
@@ -311,4 +341,5 @@ TORCH_LIBRARY_IMPL(npu, CUDA, m) {
   m.impl("cascade_suffix_decode", TORCH_FN(cascade_torch::cascade_suffix_decode));
   m.impl("cascade_lse_merge", TORCH_FN(cascade_torch::cascade_lse_merge));
   m.impl("cascade_gateup_swiglu", TORCH_FN(cascade_torch::cascade_gateup_swiglu));
+  m.impl("cascade_decode_step", TORCH_FN(cascade_torch::cascade_decode_step));
 }
