@@ -39,16 +39,30 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(co
   for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (m != -INFINITY) {
-    for (int i = 0; i < n; ++i) {
-      const float w = __shfl_sync(0xffffffffu, i < 32 ? wa : wb, i & 31);
-      if (w == 0.f) continue;
-      const float* src = i < p.n1 ? p.o1 + (static_cast<int64_t>(i) * p.rows + row) * kHeadDim
-                                  : p.o2 + (static_cast<int64_t>(i - p.n1) * p.rows + row) * kHeadDim;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(src) + lane);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
+    // batches of 8 partials: all loads of a batch are in flight together
+    for (int i0 = 0; i0 < n; i0 += 8) {
+      float w[8];
+      float4 v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = i0 + k;
+        w[k] = __shfl_sync(0xffffffffu, i < 32 ? wa : wb, i & 31);
+        v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n && w[k] != 0.f) {
+          const float* src = i < p.n1 ? p.o1 + (static_cast<int64_t>(i) * p.rows + row) * kHeadDim
+                                      : p.o2 + (static_cast<int64_t>(i - p.n1) * p.rows + row) * kHeadDim;
+          v[k] = __ldg(reinterpret_cast<const float4*>(src) + lane);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (i0 + k < n && w[k] != 0.f) {
+          acc.x += w[k] * v[k].x;
+          acc.y += w[k] * v[k].y;
+          acc.z += w[k] * v[k].z;
+          acc.w += w[k] * v[k].w;
+        }
+      }
     }
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;

@@ -45,6 +45,7 @@ struct GemmCfg {
   static constexpr int kStagingOff = kStages * kStageBytes;   // [128 rows x BN] bf16, SW128 halves
   static constexpr int kStagingBytes = kBM * BN * 2;
   static constexpr int kBarOff = kStagingOff + kStagingBytes;
+  static_assert(kBarOff % 16 == 0, "mbarriers need 8-byte alignment");
   static constexpr int kSmem = kBarOff + 256 + 1024;
   static constexpr uint32_t kTmemCols = 4 * BN;           // 2 accumulators x 2BN columns
 };
@@ -290,9 +291,179 @@ cudaError_t launch_bn(const GateUpLaunch& L, const void* a, const void* b, cudaS
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Small-M variant (M <= 128, the weight-streaming regime): swap the operands so
+// the paired weight tile fills the 128-row MMA side. D^T[128 x MP] =
+// W_tile[128 x K] X^T[K x MP], W_tile = gate rows [n0, n0+64) followed by the
+// same up rows [I+n0, I+n0+64); MP = M rounded up to 16. One 64-column output
+// tile per CTA (I/64 CTAs, two per SM), so every SM streams weights; TMEM
+// lanes 0-63 hold gate, 64-127 up; the up half is handed to the gate warps
+// through shared memory; D^T is transposed into swizzled smem and TMA-stored
+// (rows past M clipped).
+// ---------------------------------------------------------------------------
+template <int MP>
+struct SwapCfg {
+  static constexpr int kStages = MP <= 64 ? 3 : 2;
+  static constexpr int kABytes = 128 * kBK * 2;            // W tile: 16 KB
+  static constexpr int kBBytes = MP * kBK * 2;             // X tile
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStagingOff = kStages * kStageBytes;  // [MP rows][64 cols] bf16, SW128
+  static constexpr int kStagingBytes = MP * 128;
+  static constexpr int kXchgOff = kStagingOff + kStagingBytes;  // up values [64][16] fp32
+  static constexpr int kXchgBytes = 64 * 16 * 4;
+  static constexpr int kBarOff = kXchgOff + kXchgBytes;
+  static_assert(kBarOff % 16 == 0, "mbarriers need 8-byte alignment");
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static constexpr uint32_t kTmemCols = MP < 32 ? 32 : MP;
+};
+
+struct __align__(8) SwapBars {
+  uint64_t full[3];
+  uint64_t empty[3];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+
+template <int MP>
+__global__ void __launch_bounds__(kThreads, 2) gateup_swap_kernel(const __grid_constant__ GemmParams p) {
+  using C = SwapCfg<MP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  SwapBars* bars = reinterpret_cast<SwapBars*>(smem + C::kBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
+      const uint64_t pol = policy_evict_first();  // weights are streamed once
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int st = kb % C::kStages;
+        if (kb >= C::kStages) mbar_wait(&bars->empty[st], ((kb / C::kStages) - 1) & 1);
+        uint8_t* sa = smem + st * C::kStageBytes;
+        uint8_t* sb = sa + C::kABytes;
+        mbar_arrive_expect_tx(&bars->full[st], C::kStageBytes);
+        tma_load_2d_hint(sa, &p.tm_b, &bars->full[st], kb * kBK, n0, pol);               // gate rows
+        tma_load_2d_hint(sa + 64 * 128, &p.tm_b, &bars->full[st], kb * kBK, p.I + n0, pol);  // up rows
+        tma_load_2d(sb, &p.tm_a, &bars->full[st], kb * kBK, 0);                           // X rows
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(128, MP, 1, 0, 0);
+      const uint32_t sbase = smem_u32(smem);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int st = kb % C::kStages;
+        mbar_wait(&bars->full[st], (kb / C::kStages) & 1);
+        tc_fence_after();
+        const uint32_t a0 = sbase + st * C::kStageBytes;
+        const uint32_t b0 = a0 + C::kABytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          umma_f16_ss(tbase, make_smem_desc(a0 + k * 32, 16, 1024, 2), make_smem_desc(b0 + k * 32, 16, 1024, 2),
+                      idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars->empty[st]);
+      }
+      umma_commit(&bars->acc_full);
+    }
+  } else {
+    // epilogue warps 2-5: TMEM lane quarter q = warp & 3 (2,3 -> up rows; 0,1 -> gate rows)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int etid = threadIdx.x - 64;
+    float* xchg = reinterpret_cast<float*>(smem + C::kXchgOff);   // [64][16]
+    uint8_t* stg = smem + C::kStagingOff;
+    mbar_wait(&bars->acc_full, 0);
+    tc_fence_after();
+#pragma unroll 1
+    for (int c = 0; c < MP / 16; ++c) {
+      uint32_t v[16];
+      tmem_ld_32x32b_x16(tbase + lane_off + c * 16, v);
+      tmem_wait_ld();
+      if (r >= 64) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xchg[(r - 64) * 16 + j] = __uint_as_float(v[j]);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (r < 64) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = c * 16 + j;
+          const float h = silu_mul(__uint_as_float(v[j]), xchg[r * 16 + j]);
+          __nv_bfloat16 hb = __float2bfloat16_rn(h);
+          // staging row m (token), column r (output col), 128-byte swizzle
+          *reinterpret_cast<__nv_bfloat16*>(stg + m * 128 + (((r >> 3) ^ (m & 7)) << 4) + (r & 7) * 2) = hb;
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
+    tc_fence_before();
+    fence_proxy_async_smem();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (etid == 0) {
+      tma_store_2d(&p.tm_d, stg, n0, 0);
+      bulk_commit_group();
+      bulk_wait_group0();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::kTmemCols);
+  }
+}
+
+template <int MP>
+cudaError_t launch_swap(const GateUpLaunch& L, const void* a, const void* b, cudaStream_t stream) {
+  using C = SwapCfg<MP>;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = L.M;
+  p.K = L.K;
+  p.I = L.I;
+  p.num_kb = (L.K + kBK - 1) / kBK;
+  p.mode = 1;
+  if (!enc(&p.tm_a, a, L.K, L.M, static_cast<uint64_t>(L.K) * 2, MP)) return cudaErrorInvalidValue;
+  if (!enc(&p.tm_b, b, L.K, 2ull * L.I, static_cast<uint64_t>(L.K) * 2, 64)) return cudaErrorInvalidValue;
+  if (!enc(&p.tm_d, L.d, L.I, L.M, static_cast<uint64_t>(L.d_stride) * 2, MP)) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(gateup_swap_kernel<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  gateup_swap_kernel<MP><<<L.I / 64, kThreads, C::kSmem, stream>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_gateup(const GateUpLaunch& L, const void* a, const void* b, cudaStream_t stream) {
+  // fused SwiGLU with few rows: weight streaming over all SMs
+  if (L.mode == 1 && L.M <= 128) {
+    if (L.M <= 16) return launch_swap<16>(L, a, b, stream);
+    if (L.M <= 32) return launch_swap<32>(L, a, b, stream);
+    if (L.M <= 64) return launch_swap<64>(L, a, b, stream);
+    return launch_swap<128>(L, a, b, stream);
+  }
   return launch_bn<128>(L, a, b, stream);
 }
 

@@ -45,7 +45,10 @@ constexpr int kOffK = kOffQ + kTileBytes;
 constexpr int kOffV = kOffK + 2 * kTileBytes;
 constexpr int kOffP = kOffV + 2 * kTileBytes;
 constexpr int kOffAux = kOffP + kTileBytes;   // dm[2][128], l[128], m[128], barriers
-constexpr int kSmemBytes = kOffAux + 4 * 128 * 4 + 256 + 1024;
+constexpr int kBtCache = 256;                 // block-table entries of one split kept in smem
+constexpr int kOffBars = kOffAux + 4 * 128 * 4 + kBtCache * 4;
+static_assert(kOffBars % 16 == 0, "mbarriers need 8-byte alignment");
+constexpr int kSmemBytes = kOffBars + 256 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
 
@@ -115,7 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
   float* dmbuf = reinterpret_cast<float*>(smem + kOffAux);   // [2][128]
   float* lbuf = dmbuf + 2 * kRows;                            // [128]
   float* mbuf = lbuf + kRows;                                 // [128]
-  PrefixBars* bars = reinterpret_cast<PrefixBars*>(mbuf + kRows);
+  int32_t* btc = reinterpret_cast<int32_t*>(mbuf + kRows);   // [kBtCache]
+  PrefixBars* bars = reinterpret_cast<PrefixBars*>(btc + kBtCache);
 
   const int split = blockIdx.x;
   const int g = blockIdx.y % p.kv_heads;
@@ -190,14 +194,23 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
+    // the split's block-table entries -> smem first (one round trip for the
+    // warp instead of a dependent load per tile)
+    const int bs = p.block_size;
+    const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
+    const int npages = (kv + bs - 1) / bs;
+    const int first_page = s_begin / bs;
+    const int nbt = min(npages, (s_end + bs - 1) / bs) - first_page;
+    const bool cached = nbt <= kBtCache;
+    if (cached) {
+      for (int i = lane; i < nbt; i += 32) btc[i] = bt[first_page + i];
+    }
+    __syncwarp();
     if (lane == 0) {
       tma_prefetch_desc(&p.tmap_k);
       tma_prefetch_desc(&p.tmap_v);
-      const int bs = p.block_size;
       const int box_rows = bs < kTok ? bs : kTok;
       const int oob_row = p.num_blocks * bs;
-      const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
-      const int npages = (kv + bs - 1) / bs;
       const int x0 = g * kHeadDim;
       for (int j = 0; j < ntiles; ++j) {
         const int st = j & 1, u = j >> 1;
@@ -212,7 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
           for (int off = 0; off < kTok; off += box_rows) {
             const int t = t_tile + off;
             const int page = t / bs;
-            const int row = page < npages ? bt[page] * bs + (t % bs) : oob_row;
+            const int row =
+                page < npages ? (cached ? btc[page - first_page] : bt[page]) * bs + (t % bs) : oob_row;
             tma_load_2d(dst + off * 128, tm, full, x0, row);
             tma_load_2d(dst + kHalf + off * 128, tm, full, x0 + 64, row);
           }
