@@ -65,10 +65,10 @@ def _desc(**kw):
 
 def test_planner_kernel_choice_and_splits():
     from cascade_kernel import capi
-    # C2 suffix: q_len 1, group 4 -> decode path, 256-token splits
+    # C2 suffix: q_len 1, group 4 -> decode path, 512-token splits
     p = capi.plan(_desc(), 1, True)
-    assert (p.kernel, p.rows_per_group, p.split_tokens, p.num_splits) == (0, 4, 256, 4)
-    assert p.workspace_bytes == 4 * 64 * 32 * 129 * 4
+    assert (p.kernel, p.rows_per_group, p.split_tokens, p.num_splits) == (0, 4, 512, 2)
+    assert p.workspace_bytes == 2 * 64 * 32 * 129 * 4
     # C2 stage-1: one flattened request of 64 tokens -> 256 rows -> tcgen05 path
     p = capi.plan(_desc(num_tokens=64, batch=1, block_cols=32, q_seqlen_value=64), 64, False)
     assert p.kernel == 1 and p.rows_per_group == 256 and p.split_tokens % 128 == 0

@@ -126,7 +126,9 @@ def test_suffix_decode_block_sizes(dtype, bs):
     dev, host = _rand_case(len(kv), 10, 2, bs, kv, 1, dtype, seed=bs)
     out, lse = Hh.run_capi_paged(*dev, 1, suffix=True)
     qf, kf, vf, bt, qs, kvs = host
-    seg = lambda n: O.decode_segments(n, split=256, tile=64, warps=4)
+    C = Hh.capi()
+    split = C.plan(C.paged_desc(*dev, 1), 1, True).split_tokens
+    seg = lambda n: O.decode_segments(n, split=split, tile=64, warps=4)
     o_ks, l_ks, A = O.paged_attention_ref(qf, kf, vf, bt, qs, kvs, segments=seg, p_dtype=dtype,
                                           with_tieband=True, tieband_rule="rescaled")
     o = Hh.dev_to_f64(out)

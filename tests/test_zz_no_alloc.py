@@ -55,7 +55,7 @@ def _noalloc(args):
 def test_noalloc_matches_allocating_entry_on_two_calls():
     Hh.need_cuda()
     C = Hh.capi()
-    # two different problems, both split over several 256-token partials
+    # two different problems, both split into several KV partials
     cases = [_case(11, B=64, kv_max=1024), _case(12, B=40, kv_max=768, H=40)]
     for args in cases:
         desc = C.paged_desc(*args, 1)
@@ -79,7 +79,7 @@ def test_noalloc_refuses_oversized_and_legacy_calls():
     small = _case(14, B=4, kv_max=300)
     out = torch.full_like(small[0], 3.0)
     lse = torch.empty(small[0].shape[0] * small[0].shape[1], dtype=torch.float32, device="cuda")
-    # 512 requests x 32 heads x 16 splits of 4096 tokens x 516 B > 16 MiB; the
+    # 512 requests x 32 heads x several splits of 4096 tokens x 516 B > 16 MiB; the
     # size check runs on the shapes before anything is launched
     big = C.paged_desc(None, None, None, None, None, None, 1,
                        shape=dict(num_tokens=512, num_heads=32, head_dim=128, num_blocks=1, block_size=128,

@@ -58,7 +58,7 @@ bool block_size_ok(int64_t bs) {
   return bs == 16 || bs == 32 || bs == 64 || bs == 128 || bs == 256 || bs == 512;
 }
 
-constexpr int kDecodeSplit = 256;  // kv tokens per decode split (multiple of its 64-token tile)
+constexpr int kDecodeSplit = 512;  // kv tokens per decode split (multiple of its 64-token tile)
 constexpr int kTcTile = 128;       // kv tokens per tcgen05 tile
 constexpr int kMaxSplits = 32;     // per request; the step combine merges up to 64 partials per row
 

@@ -22,13 +22,25 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(co
   const int lane = threadIdx.x & 31;
   if (row >= p.rows) return;
   const int n = p.n1 + p.n2;
-  // lse of every partial (n <= 64: two per lane)
+  // Every load of the row is issued before any result is needed: the lse of
+  // partial `lane` / `lane+32`, and this lane's 4 dims of the first 16
+  // partials. A partial with lse = -inf may hold anything: it is selected
+  // out, never multiplied.
+  auto part_ptr = [&](int i) -> const float4* {
+    const float* base = i < p.n1 ? p.o1 + (static_cast<int64_t>(i) * p.rows + row) * kHeadDim
+                                 : p.o2 + (static_cast<int64_t>(i - p.n1) * p.rows + row) * kHeadDim;
+    return reinterpret_cast<const float4*>(base) + lane;
+  };
   float la = -INFINITY, lb = -INFINITY;
   if (lane < n) la = lane < p.n1 ? p.l1[lane * p.rows + row] : p.l2[(lane - p.n1) * p.rows + row];
   if (lane + 32 < n) {
     const int i = lane + 32;
     lb = i < p.n1 ? p.l1[i * p.rows + row] : p.l2[(i - p.n1) * p.rows + row];
   }
+  constexpr int kPre = 16;
+  float4 v[kPre];
+#pragma unroll
+  for (int k = 0; k < kPre; ++k) v[k] = k < n ? __ldg(part_ptr(k)) : make_float4(0.f, 0.f, 0.f, 0.f);
   float m = fmaxf(la, lb);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -38,32 +50,19 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(co
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (m != -INFINITY) {
-    // batches of 8 partials: all loads of a batch are in flight together
-    for (int i0 = 0; i0 < n; i0 += 8) {
-      float w[8];
-      float4 v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = i0 + k;
-        w[k] = __shfl_sync(0xffffffffu, i < 32 ? wa : wb, i & 31);
-        v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n && w[k] != 0.f) {
-          const float* src = i < p.n1 ? p.o1 + (static_cast<int64_t>(i) * p.rows + row) * kHeadDim
-                                      : p.o2 + (static_cast<int64_t>(i - p.n1) * p.rows + row) * kHeadDim;
-          v[k] = __ldg(reinterpret_cast<const float4*>(src) + lane);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (i0 + k < n && w[k] != 0.f) {
-          acc.x += w[k] * v[k].x;
-          acc.y += w[k] * v[k].y;
-          acc.z += w[k] * v[k].z;
-          acc.w += w[k] * v[k].w;
-        }
-      }
+  auto add = [&](float w, const float4& x) {
+    if (w != 0.f) {
+      acc.x += w * x.x;
+      acc.y += w * x.y;
+      acc.z += w * x.z;
+      acc.w += w * x.w;
     }
+  };
+#pragma unroll
+  for (int k = 0; k < kPre; ++k) add(__shfl_sync(0xffffffffu, wa, k), v[k]);
+  for (int i = kPre; i < n; ++i) {  // rare: more than 16 partials per row
+    const float w = __shfl_sync(0xffffffffu, i < 32 ? wa : wb, i & 31);
+    if (w != 0.f) add(w, __ldg(part_ptr(i)));
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   const int64_t o = row * kHeadDim + lane * 4;
