@@ -65,3 +65,34 @@ def cascade_decode(q, k_pool, v_pool, tables: CascadeTables, out_dtype=None, fus
     if reference_domain:
         return npu.lse_merge(o1, o2, l1, l2, code)
     return npu.cascade_lse_merge(o1, o2, l1, l2, code)
+
+
+class CascadeStepGraph:
+    """A cascade decode step captured once in a CUDA graph and replayed.
+
+    The step's inputs live in fixed device buffers (``q``, the pools and the
+    ``tables`` given at construction); a serving loop writes the next step's
+    queries and index tensors into them in place and calls ``replay()``,
+    which re-issues the stage-1, suffix and combine kernels without any host
+    work. Requires the uniform-q path (``tables.uniform_group > 0``): the
+    per-request path reads seqlens back to the host and cannot be captured.
+    """
+
+    def __init__(self, q, k_pool, v_pool, tables: CascadeTables, out_dtype=None, warmup=2):
+        if tables.uniform_group <= 0:
+            raise ValueError("CascadeStepGraph needs uniform prefix groups (tables.uniform_group > 0)")
+        self.q, self.k_pool, self.v_pool, self.tables = q, k_pool, v_pool, tables
+        self.out_dtype = out_dtype
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+
+    def replay(self):
+        self.graph.replay()
+        return self.out

@@ -260,6 +260,20 @@ bool encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
   return r == CUDA_SUCCESS;
 }
 
+cudaError_t ensure_smem_limit(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<const void*, int>, int>> done;  // ((kernel, device), bytes)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (d.first.first == kernel && d.first.second == dev && d.second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.push_back({{kernel, dev}, bytes});
+  return e;
+}
+
 int set_error(int code, const char* msg) {
   g_last_error = msg;
   return code;

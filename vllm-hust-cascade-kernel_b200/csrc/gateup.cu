@@ -285,7 +285,7 @@ cudaError_t launch_bn(const GateUpLaunch& L, const void* a, const void* b, cudaS
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = p.num_m * p.num_n;
   const int grid = tiles < sms ? tiles : sms;
-  cudaError_t e = cudaFuncSetAttribute(gateup_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gateup_kernel<BN>), C::kSmem);
   if (e != cudaSuccess) return e;
   gateup_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(p);
   return cudaGetLastError();
@@ -448,7 +448,7 @@ cudaError_t launch_swap(const GateUpLaunch& L, const void* a, const void* b, cud
   if (!enc(&p.tm_a, a, L.K, L.M, static_cast<uint64_t>(L.K) * 2, MP)) return cudaErrorInvalidValue;
   if (!enc(&p.tm_b, b, L.K, 2ull * L.I, static_cast<uint64_t>(L.K) * 2, 64)) return cudaErrorInvalidValue;
   if (!enc(&p.tm_d, L.d, L.I, L.M, static_cast<uint64_t>(L.d_stride) * 2, MP)) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(gateup_swap_kernel<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gateup_swap_kernel<MP>), C::kSmem);
   if (e != cudaSuccess) return e;
   gateup_swap_kernel<MP><<<L.I / 64, kThreads, C::kSmem, stream>>>(p);
   return cudaGetLastError();

@@ -92,6 +92,10 @@ cudaError_t launch_gateup(const GateUpLaunch& p, const void* a, const void* b, c
 cudaError_t launch_gateup_window(const void* ws, void* d, int64_t d_stride, int32_t M, int32_t I, int32_t mode,
                                  cudaStream_t stream);
 
+// Host: raise a kernel's dynamic shared memory limit once per (kernel,
+// device) instead of on every launch.
+cudaError_t ensure_smem_limit(const void* kernel, int bytes);
+
 // Host: record `msg` as this thread's cascade_last_error() text; returns `code`.
 int set_error(int code, const char* msg);
 

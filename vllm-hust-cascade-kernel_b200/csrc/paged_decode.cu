@@ -427,7 +427,7 @@ __global__ void split_combine_kernel(const __grid_constant__ PagedAttnLaunch p) 
 cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream) {
   dim3 grid(p.num_splits, p.kv_heads, p.batch);
   auto kern = fp16 ? paged_decode_kernel<true> : paged_decode_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();

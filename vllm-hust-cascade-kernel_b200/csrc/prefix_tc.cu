@@ -439,7 +439,7 @@ cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStre
   const int mtiles = (p.max_q_seqlen * p.group + kRows - 1) / kRows;
   dim3 grid(p.num_splits, p.kv_heads * mtiles, p.batch);
   auto kern = fp16 ? paged_prefix_tc_kernel<true> : paged_prefix_tc_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
