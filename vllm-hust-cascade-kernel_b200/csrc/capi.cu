@@ -391,10 +391,18 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
   if ((pa.num_splits ? La.num_splits : 0) + (pb.num_splits ? Lb.num_splits : 0) > 64)
     return fail(CASCADE_ERR_UNSUPPORTED, "%s: more than 64 KV splits per row", op);
   cudaError_t e = cudaSuccess;
-  if (pa.num_splits) e = launch_attention(La, pa.kernel, fp16, st);
-  if (e == cudaSuccess && pb.num_splits) e = launch_attention(Lb, pb.kernel, fp16, st);
+  // The suffix decode (the long KV stream) goes first; stage-1 is launched as
+  // its programmatic dependent, so its CTAs take over SMs as the decode's
+  // ragged tail drains instead of waiting for the whole grid, and the combine
+  // is the programmatic dependent of stage-1 (each kernel's CTAs wait for the
+  // kernel before them only when they exit; the combine waits at its start).
+  if (pb.num_splits) e = launch_attention(Lb, pb.kernel, fp16, st);
+  La.pdl = pb.num_splits ? 1 : 0;
+  if (e == cudaSuccess && pa.num_splits) e = launch_attention(La, pa.kernel, fp16, st);
   if (e == cudaSuccess) {
     CascadeCombineLaunch C;
+    std::memset(&C, 0, sizeof(C));
+    C.pdl = (pa.num_splits || pb.num_splits) ? 1 : 0;
     C.o1 = La.part_o;
     C.l1 = La.part_lse;
     C.n1 = pa.num_splits ? La.num_splits : 0;

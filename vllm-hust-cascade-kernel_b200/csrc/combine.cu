@@ -20,6 +20,7 @@ constexpr int kWarpsPerBlock = 8;
 __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(const CascadeCombineLaunch p) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  if (p.pdl) pdl_wait();  // partials come from the kernels before this one
   if (row >= p.rows) return;
   const int n = p.n1 + p.n2;
   // Every load of the row is issued before any result is needed: the lse of
@@ -83,8 +84,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(co
 cudaError_t launch_cascade_combine(const CascadeCombineLaunch& p, cudaStream_t stream) {
   if (p.rows == 0) return cudaSuccess;
   const unsigned blocks = static_cast<unsigned>((p.rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
-  cascade_combine_kernel<<<blocks, kWarpsPerBlock * 32, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_maybe_pdl(cascade_combine_kernel, dim3(blocks), dim3(kWarpsPerBlock * 32), 0, stream, p.pdl != 0, p);
 }
 
 }  // namespace cascade

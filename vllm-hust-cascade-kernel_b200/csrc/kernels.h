@@ -32,10 +32,33 @@ struct PagedAttnLaunch {
   int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
   int32_t lse_stride;   // 8 (reference padded rows) or 1 (compact)
   int32_t partial_out;  // 1: always write split partials (a later combine produces the output)
+  int32_t pdl;          // 1: launched as a programmatic dependent of the previous kernel in the stream
   float scale_log2;     // softmax scale * log2(e)
 };
 
 cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream);
+
+// Launch `kern` with the programmatic-dependent attribute when `pdl` is set.
+template <typename Arg>
+cudaError_t launch_maybe_pdl(void (*kern)(Arg), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                             const Arg& arg) {
+  if (!pdl) {
+    kern<<<grid, block, smem, stream>>>(arg);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, arg);
+}
+
 
 // Stage-1 tensor-core path (tcgen05, > 16 rows per (request, kv head)).
 cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream);
@@ -55,6 +78,7 @@ struct CascadeCombineLaunch {
   void* out;            // [rows][128] in out_dtype
   int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
   float* lse_out;       // [rows] or null
+  int32_t pdl;          // 1: launched as a programmatic dependent (waits for its primary first)
 };
 
 cudaError_t launch_cascade_combine(const CascadeCombineLaunch& p, cudaStream_t stream);

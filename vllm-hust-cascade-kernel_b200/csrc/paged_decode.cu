@@ -65,7 +65,7 @@ __device__ __forceinline__ void store_out(void* out, int out_dtype, size_t idx, 
 }
 
 template <bool kFp16>
-__global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_constant__ PagedAttnLaunch p) {
+__device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   DecodeBarriers* bars = reinterpret_cast<DecodeBarriers*>(smem + kStages * kStageBytes);
@@ -378,6 +378,13 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
   }
 }
 
+template <bool kFp16>
+__global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_constant__ PagedAttnLaunch p) {
+  pdl_launch_dependents();
+  paged_decode_body<kFp16>(p);
+  if (p.pdl && threadIdx.x == 0) pdl_wait();
+}
+
 // One warp per (token, head) row: merge the split partials.
 __global__ void split_combine_kernel(const __grid_constant__ PagedAttnLaunch p) {
   const int warps_per_block = blockDim.x >> 5;
@@ -429,8 +436,7 @@ cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_
   auto kern = fp16 ? paged_decode_kernel<true> : paged_decode_kernel<false>;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  return launch_maybe_pdl(kern, grid, dim3(kThreads), kSmemBytes, stream, p.pdl != 0, p);
 }
 
 cudaError_t launch_split_combine(const PagedAttnLaunch& p, cudaStream_t stream) {

@@ -112,7 +112,7 @@ __device__ __forceinline__ void store_chunk(const PagedAttnLaunch& p, size_t ele
 }
 
 template <bool kFp16>
-__global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __grid_constant__ PagedAttnLaunch p) {
+__device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* dmbuf = reinterpret_cast<float*>(smem + kOffAux);   // [2][128]
@@ -433,6 +433,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
   }
 }
 
+template <bool kFp16>
+__global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __grid_constant__ PagedAttnLaunch p) {
+  pdl_launch_dependents();
+  paged_prefix_tc_body<kFp16>(p);
+  if (p.pdl && threadIdx.x == 0) pdl_wait();
+}
+
 }  // namespace
 
 cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream) {
@@ -441,8 +448,7 @@ cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStre
   auto kern = fp16 ? paged_prefix_tc_kernel<true> : paged_prefix_tc_kernel<false>;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  return launch_maybe_pdl(kern, grid, dim3(kThreads), kSmemBytes, stream, p.pdl != 0, p);
 }
 
 }  // namespace cascade

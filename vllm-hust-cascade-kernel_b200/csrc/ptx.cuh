@@ -74,6 +74,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// ----------------------------------------------- programmatic launch ----
+// Kernels of a cascade step may run as programmatic dependents of the kernel
+// before them in the stream (cudaLaunchAttributeProgrammaticStreamSerialization).
+// Every kernel signals at its start that its dependents may be scheduled; a
+// dependent whose inputs do not come from its primary never waits at the
+// start, but one thread of each of its CTAs waits for the primary's
+// completion before exiting, so "this grid completed" still implies "every
+// grid before it completed" for whatever follows in the stream.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA ----
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* desc) {
