@@ -37,6 +37,7 @@ sys.path.insert(0, os.path.join(ROOT, "vllm-hust-cascade-kernel_b200"))
 
 METRIC = "cascade decode attention HBM GB/s (Llama-3-8B cascade step, B=64, prefix 4096)"
 FLUSH_BYTES = 256 * 1024 * 1024
+DECODE_TRAFFIC_BYTES = 162_838_528 + 4_104_960   # ncu dram__bytes_read.sum + dram__bytes_write.sum
 
 
 class L2Flush:
@@ -46,7 +47,7 @@ class L2Flush:
 
     def __init__(self, torch):
         self.w = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
-        self.r = torch.zeros(FLUSH_BYTES // 4, dtype=torch.int32, device="cuda")
+        self.r = torch.zeros(FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
 
     def __call__(self):
         self.w.zero_()
@@ -293,7 +294,10 @@ def run_ours(args, rank, world, local):
             "peak": peaks["hbm_gbs"],
             "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4),
-            "traffic": None,
+            # DRAM bytes (read + write) of one launch of this kernel from the ncu
+            # capture summarised in profiles/paged_decode_kernel_c2.txt
+            "traffic": DECODE_TRAFFIC_BYTES,
+            "traffic_src": "ncu capture (profiles/paged_decode_kernel_c2.txt)",
             "peak_src": peaks["src"],
         },
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
