@@ -3,7 +3,7 @@
 // small-row forms of the stage-1 op.
 //
 // Memory-bound design (KV bytes dominate):
-//  * one CTA per (split of 256 kv tokens, kv head, request); the split's
+//  * one CTA per (split of 512 kv tokens, kv head, request); the split's
 //    partial (O, LSE) is merged by launch_split_combine when a request has
 //    more than one split;
 //  * a producer warp streams 64-token K/V tiles with 2-D TMA (one box per page
@@ -76,11 +76,23 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int kv = static_cast<int>(p.kv_seqlens[b]);
+  // The split's block-table entries do not depend on the kv length: the
+  // producer warp issues their load first, so it overlaps the length load.
+  const int s_begin = split * p.split_tokens;
+  const int first_page = s_begin / p.block_size;
+  const int bt_avail = min(kBtCache, p.block_cols - first_page);
+  int bt_pre0 = 0, bt_pre1 = 0;
+  if (warp == kConsumerWarps) {
+    const int32_t* btrow = p.block_table + static_cast<size_t>(b) * p.block_cols + first_page;
+    if (lane < bt_avail) bt_pre0 = btrow[lane];
+    if (lane + 32 < bt_avail) bt_pre1 = btrow[lane + 32];
+  }
+
+  // kv is clamped to the block table's capacity, so no entry past a row is read
+  const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
   const int q_len = p.q_seqlen_value > 0 ? p.q_seqlen_value : static_cast<int>(p.q_seqlens[b]);
   const int nrows = q_len * p.group;
   const int tok0 = request_token_offset(p, b);
-  const int s_begin = split * p.split_tokens;
   const int s_end = min(kv, s_begin + p.split_tokens);
   const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
 
@@ -125,12 +137,13 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
     const int bs = p.block_size;
     const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
     const int npages = (kv + bs - 1) / bs;
-    const int first_page = s_begin / bs;
     const int last_page = min(npages, (s_end + bs - 1) / bs);  // exclusive
     const int nbt = last_page - first_page;
     const bool cached = nbt <= kBtCache;
     if (cached) {
-      for (int i = lane; i < nbt; i += 32) bars->bt[i] = bt[first_page + i];
+      static_assert(kBtCache <= 64, "two prefetched entries per lane");
+      if (lane < nbt) bars->bt[lane] = bt_pre0;
+      if (lane + 32 < nbt) bars->bt[lane + 32] = bt_pre1;
     }
     __syncwarp();
     if (lane == 0) {
@@ -309,14 +322,22 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
   // All tiles are consumed (every full barrier was waited by every warp), so
   // the stage ring is free once all consumer warps reach this barrier.
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  float* so = reinterpret_cast<float*>(smem);                 // [4][16][128]
-  float* sm = so + kConsumerWarps * 16 * kHeadDim;            // [4][16]
+  // Rows are padded to 136 floats: the 8 rows of one fragment store then fall
+  // on distinct banks (row r starts at bank 8r mod 32), and only the query
+  // rows that exist are written.
+  constexpr int kSoStride = kHeadDim + 8;
+  float* so = reinterpret_cast<float*>(smem);                 // [4][16][kSoStride]
+  float* sm = so + kConsumerWarps * 16 * kSoStride;           // [4][16]
   float* sl = sm + kConsumerWarps * 16;                       // [4][16]
+  if (gq < nrows) {
+    float* dst = so + (warp * 16 + gq) * kSoStride + 2 * tq;
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const int d = n * 8 + 2 * tq;
-    *reinterpret_cast<float2*>(&so[(warp * 16 + gq) * kHeadDim + d]) = make_float2(o[n][0], o[n][1]);
-    *reinterpret_cast<float2*>(&so[(warp * 16 + gq + 8) * kHeadDim + d]) = make_float2(o[n][2], o[n][3]);
+    for (int n = 0; n < 16; ++n) *reinterpret_cast<float2*>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
+  }
+  if (gq + 8 < nrows) {
+    float* dst = so + (warp * 16 + gq + 8) * kSoStride + 2 * tq;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) *reinterpret_cast<float2*>(dst + n * 8) = make_float2(o[n][2], o[n][3]);
   }
   if (tq == 0) {
     sm[warp * 16 + gq] = m0;
@@ -326,11 +347,12 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
-  // 128 threads: thread -> (row = tid / 8, 16 dims); 16 rows x 8 threads
+  // 128 threads, one float4 of one row each: a warp covers one 512-byte row
+  // (conflict-free smem reads, coalesced global stores).
   const int tid = threadIdx.x;
-  const int r = tid >> 3;
-  const int d0 = (tid & 7) * 16;
-  if (r < nrows) {
+  for (int idx = tid; idx < nrows * (kHeadDim / 4); idx += kConsumerWarps * 32) {
+    const int r = idx / (kHeadDim / 4);
+    const int d0 = (idx % (kHeadDim / 4)) * 4;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm[w * 16 + r]);
@@ -345,35 +367,25 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
     const float lse_nat = (wsum > 0.f) ? (M + log2f(wsum)) * 0.6931471805599453f : -INFINITY;
     const int t = tok0 + r / p.group, h = g * p.group + r % p.group;
     const size_t row = static_cast<size_t>(t) * p.num_heads + h;
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) {
       if (wt[w] == 0.f) continue;
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(&so[(w * 16 + r) * kHeadDim + d0 + j]);
-        acc[j] += wt[w] * v.x;
-        acc[j + 1] += wt[w] * v.y;
-        acc[j + 2] += wt[w] * v.z;
-        acc[j + 3] += wt[w] * v.w;
-      }
+      const float4 v = *reinterpret_cast<const float4*>(&so[(w * 16 + r) * kSoStride + d0]);
+      acc.x += wt[w] * v.x;
+      acc.y += wt[w] * v.y;
+      acc.z += wt[w] * v.z;
+      acc.w += wt[w] * v.w;
     }
+    const int c = idx % (kHeadDim / 4);
     if (p.num_splits > 1 || p.partial_out) {
       float* dst = p.part_o + (static_cast<size_t>(split) * p.num_tokens * p.num_heads + row) * kHeadDim + d0;
-#pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4*>(dst + j) =
-            make_float4(acc[j] * inv, acc[j + 1] * inv, acc[j + 2] * inv, acc[j + 3] * inv);
-      if ((tid & 7) == 0) p.part_lse[static_cast<size_t>(split) * p.num_tokens * p.num_heads + row] = lse_nat;
+      *reinterpret_cast<float4*>(dst) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+      if (c == 0) p.part_lse[static_cast<size_t>(split) * p.num_tokens * p.num_heads + row] = lse_nat;
     } else {
-#pragma unroll
-      for (int j = 0; j < 16; j += 2)
-        store_out<kFp16>(p.out, p.out_dtype, row * kHeadDim + d0 + j, acc[j] * inv, acc[j + 1] * inv);
-      if ((tid & 7) < p.lse_stride) {
-        for (int c = tid & 7; c < p.lse_stride; c += 8) p.lse[row * p.lse_stride + c] = lse_nat;
-      }
+      store_out<kFp16>(p.out, p.out_dtype, row * kHeadDim + d0, acc.x * inv, acc.y * inv);
+      store_out<kFp16>(p.out, p.out_dtype, row * kHeadDim + d0 + 2, acc.z * inv, acc.w * inv);
+      for (int cc = c; cc < p.lse_stride; cc += kHeadDim / 4) p.lse[row * p.lse_stride + cc] = lse_nat;
     }
   }
 }
