@@ -129,7 +129,8 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
 
-  const int kv = static_cast<int>(p.kv_seqlens[b]);
+  // kv is clamped to the block table's capacity, so no entry past a row is read
+  const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
   const int q_len = p.q_seqlen_value > 0 ? p.q_seqlen_value : static_cast<int>(p.q_seqlens[b]);
   const int nrows = q_len * p.group;
   const int row0 = mt * kRows;
