@@ -124,3 +124,44 @@ def test_decode_step_capi_and_partials_only_flag():
     C.suffix_decode(dpo, o2, l2, ws2)
     torch.cuda.synchronize()
     assert torch.all(o2 == 5.0)
+
+
+def test_step_graph_replay_with_host_io():
+    """CascadeStepGraph replays the step bit-identically to the eager op, and
+    with host_io its replay also moves fresh host inputs in and the output
+    out: changing the pinned host query between replays changes the result
+    exactly as the eager step on the new query does."""
+    import torch
+    from cascade_kernel.cascade import CascadeStepGraph, CascadeTables, cascade_decode
+    Hh.need_cuda()
+    kw = dict(CASES["c2_like_b16"])
+    kw["dtype"] = torch.bfloat16
+    w = _work("graph_io", **kw)
+    t = w.tables
+    parts = [w.q, t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens, t.suffix_block_table,
+             t.suffix_q_seqlens, t.suffix_kv_seqlens]
+    offs, cur = [], 0
+    for x in parts:
+        offs.append(cur)
+        cur += (x.numel() * x.element_size() + 255) // 256 * 256
+    host_in = torch.zeros(cur, dtype=torch.uint8).pin_memory()
+    def put(i, x):
+        nb = x.numel() * x.element_size()
+        host_in[offs[i]:offs[i] + nb].copy_(x.contiguous().view(-1).view(torch.uint8).cpu())
+    for i, x in enumerate(parts):
+        put(i, x)
+    dev_in = torch.empty(cur, dtype=torch.uint8, device="cuda")
+    views = [dev_in[o:o + x.numel() * x.element_size()].view(x.dtype).view(x.shape) for x, o in zip(parts, offs)]
+    dev_in.copy_(host_in)
+    tt = CascadeTables(*views[1:], uniform_group=t.uniform_group)
+    out_h = torch.empty(w.q.shape, dtype=w.q.dtype).pin_memory()
+    plain = CascadeStepGraph(views[0], w.k_pool, w.v_pool, tt)
+    io = CascadeStepGraph(views[0], w.k_pool, w.v_pool, tt, host_io=(host_in, dev_in, out_h))
+    eager = cascade_decode(w.q, w.k_pool, w.v_pool, t)
+    assert torch.equal(plain.replay(), eager)
+    for step in range(2):
+        q_new = (torch.randn(w.q.shape, device="cuda") * (1.0 + step)).to(w.q.dtype)
+        put(0, q_new)
+        io.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out_h, cascade_decode(q_new, w.k_pool, w.v_pool, t).cpu())

@@ -73,25 +73,41 @@ class CascadeStepGraph:
     The step's inputs live in fixed device buffers (``q``, the pools and the
     ``tables`` given at construction); a serving loop writes the next step's
     queries and index tensors into them in place and calls ``replay()``,
-    which re-issues the stage-1, suffix and combine kernels without any host
+    which re-issues the suffix, stage-1 and combine kernels without any host
     work. Requires the uniform-q path (``tables.uniform_group > 0``): the
     per-request path reads seqlens back to the host and cannot be captured.
+
+    ``host_io=(host_in, dev_in, host_out)`` puts the step's host traffic in
+    the same graph: every replay first copies the pinned host buffer
+    ``host_in`` into the device buffer ``dev_in`` (which must back ``q`` and
+    the tables), and after the step copies the output into the pinned host
+    tensor ``host_out``.
     """
 
-    def __init__(self, q, k_pool, v_pool, tables: CascadeTables, out_dtype=None, warmup=2):
+    def __init__(self, q, k_pool, v_pool, tables: CascadeTables, out_dtype=None, warmup=2, host_io=None):
         if tables.uniform_group <= 0:
             raise ValueError("CascadeStepGraph needs uniform prefix groups (tables.uniform_group > 0)")
         self.q, self.k_pool, self.v_pool, self.tables = q, k_pool, v_pool, tables
         self.out_dtype = out_dtype
+        self.host_io = host_io
+
+        def step():
+            if host_io is not None:
+                host_io[1].copy_(host_io[0], non_blocking=True)
+            out = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+            if host_io is not None:
+                host_io[2].copy_(out, non_blocking=True)
+            return out
+
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for _ in range(warmup):
-                cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+                step()
         torch.cuda.current_stream().wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.out = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+            self.out = step()
 
     def replay(self):
         self.graph.replay()
