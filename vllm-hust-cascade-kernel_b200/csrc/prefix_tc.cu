@@ -401,68 +401,104 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
     const float l = lbuf[r], m = mbuf[r];
     const float inv = 1.f / l;
     const float lse_nat = (m + __log2f(l)) * 0.6931471805599453f;
+    if (partial || p.out_dtype == 2) {
+      // fp32 rows: stage unswizzled with a 528-byte row pitch (conflict-free
+      // for the row-per-thread writes) and let the bulk-copy engine move each
+      // 512-byte row to global memory.
+      constexpr int kPitch = kHeadDim + 4;
+      float* stage = reinterpret_cast<float*>(smem + kOffK);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tbase + lane_off + kColO + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<float4*>(stage + r * kPitch + c * 32 + i * 4) =
+              make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                          __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (r < unit_rows) {
+        const size_t row = out_row(r);
+        float* dst = partial ? p.part_o + (static_cast<size_t>(split) * plane + row) * kHeadDim
+                             : static_cast<float*>(p.out) + row * kHeadDim;
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], 512;" ::"l"(dst),
+                     "r"(smem_u32(stage + r * kPitch))
+                     : "memory");
+        bulk_commit_group();
+        if (partial) {
+          p.part_lse[static_cast<size_t>(split) * plane + row] = lse_nat;
+        } else {
+          for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = lse_nat;
+        }
+        bulk_wait_group0();
+      }
+    } else {
     float* stage = reinterpret_cast<float*>(smem + kOffK);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t o[32];
-      tmem_ld_32x32b_x32(tbase + lane_off + kColO + c * 32, o);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        *reinterpret_cast<float4*>(stage + r * kHeadDim + (((c * 8 + i) ^ (r & 31)) << 2)) =
-            make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                        __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
-    }
-    if (r < unit_rows) {
-      const size_t row = out_row(r);
-      if (partial) {
-        p.part_lse[static_cast<size_t>(split) * plane + row] = lse_nat;
-      } else {
-        for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = lse_nat;
+  #pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tbase + lane_off + kColO + c * 32, o);
+        tmem_wait_ld();
+  #pragma unroll
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<float4*>(stage + r * kHeadDim + (((c * 8 + i) ^ (r & 31)) << 2)) =
+              make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                          __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
       }
-    }
-    asm volatile("bar.sync 2, 128;" ::: "memory");
-    // warp w of the group stores rows [32w, 32w + 32); lane = 16-byte chunk.
-    // Rows are walked as (query token, head) without divisions, 8 loads in
-    // flight before their stores.
-    {
-      const int rbeg = (warp & 3) * 32;
-      int tq_ = (row0 + rbeg) / p.group, hq_ = (row0 + rbeg) % p.group;
-      const size_t head0 = static_cast<size_t>(g) * p.group;
-#pragma unroll
-      for (int k0 = 0; k0 < 32; k0 += 8) {
-        float4 v[8];
-        size_t rows[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int rr = rbeg + k0 + k;
-          v[k] = *reinterpret_cast<const float4*>(stage + rr * kHeadDim + ((lane ^ (rr & 31)) << 2));
-          rows[k] = static_cast<size_t>(tok0 + tq_) * p.num_heads + head0 + hq_;
-          if (++hq_ == p.group) {
-            hq_ = 0;
-            ++tq_;
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (rbeg + k0 + k >= unit_rows) break;
-          const size_t row = rows[k];
-          if (partial) {
-            *reinterpret_cast<float4*>(p.part_o + (static_cast<size_t>(split) * plane + row) * kHeadDim + lane * 4) =
-                v[k];
-          } else if (p.out_dtype == 2) {
-            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * kHeadDim + lane * 4) = v[k];
-          } else {
-            const bool h = p.out_dtype == 1;
-            const uint32_t a = h ? pack2<true>(v[k].x, v[k].y) : pack2<false>(v[k].x, v[k].y);
-            const uint32_t bb = h ? pack2<true>(v[k].z, v[k].w) : pack2<false>(v[k].z, v[k].w);
-            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + row * kHeadDim + lane * 4) = make_uint2(a, bb);
-          }
+      if (r < unit_rows) {
+        const size_t row = out_row(r);
+        if (partial) {
+          p.part_lse[static_cast<size_t>(split) * plane + row] = lse_nat;
+        } else {
+          for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = lse_nat;
         }
       }
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      // warp w of the group stores rows [32w, 32w + 32); lane = 16-byte chunk.
+      // Rows are walked as (query token, head) without divisions, 8 loads in
+      // flight before their stores.
+      {
+        const int rbeg = (warp & 3) * 32;
+        int tq_ = (row0 + rbeg) / p.group, hq_ = (row0 + rbeg) % p.group;
+        const size_t head0 = static_cast<size_t>(g) * p.group;
+  #pragma unroll
+        for (int k0 = 0; k0 < 32; k0 += 8) {
+          float4 v[8];
+          size_t rows[8];
+  #pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int rr = rbeg + k0 + k;
+            v[k] = *reinterpret_cast<const float4*>(stage + rr * kHeadDim + ((lane ^ (rr & 31)) << 2));
+            rows[k] = static_cast<size_t>(tok0 + tq_) * p.num_heads + head0 + hq_;
+            if (++hq_ == p.group) {
+              hq_ = 0;
+              ++tq_;
+            }
+          }
+  #pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            if (rbeg + k0 + k >= unit_rows) break;
+            const size_t row = rows[k];
+            if (partial) {
+              *reinterpret_cast<float4*>(p.part_o + (static_cast<size_t>(split) * plane + row) * kHeadDim + lane * 4) =
+                  v[k];
+            } else if (p.out_dtype == 2) {
+              *reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * kHeadDim + lane * 4) = v[k];
+            } else {
+              const bool h = p.out_dtype == 1;
+              const uint32_t a = h ? pack2<true>(v[k].x, v[k].y) : pack2<false>(v[k].x, v[k].y);
+              const uint32_t bb = h ? pack2<true>(v[k].z, v[k].w) : pack2<false>(v[k].z, v[k].w);
+              *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + row * kHeadDim + lane * 4) = make_uint2(a, bb);
+            }
+          }
+        }
+      }
     }
-  }
-
+  
+      }
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
