@@ -424,9 +424,7 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
         const size_t row = out_row(r);
         float* dst = partial ? p.part_o + (static_cast<size_t>(split) * plane + row) * kHeadDim
                              : static_cast<float*>(p.out) + row * kHeadDim;
-        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], 512;" ::"l"(dst),
-                     "r"(smem_u32(stage + r * kPitch))
-                     : "memory");
+        bulk_store_1d(dst, stage + r * kPitch, kHeadDim * 4);
         bulk_commit_group();
         if (partial) {
           p.part_lse[static_cast<size_t>(split) * plane + row] = lse_nat;

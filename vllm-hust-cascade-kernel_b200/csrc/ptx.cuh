@@ -135,6 +135,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* desc, const void
                : "memory");
 }
 
+// Contiguous shared -> global copy by the bulk-copy engine (both addresses
+// 16-byte aligned, bytes a multiple of 16), tracked by the bulk-group wait.
+__device__ __forceinline__ void bulk_store_1d(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until all committed bulk stores of this thread have finished READING smem.
