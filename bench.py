@@ -37,7 +37,7 @@ sys.path.insert(0, os.path.join(ROOT, "vllm-hust-cascade-kernel_b200"))
 
 METRIC = "cascade decode attention HBM GB/s (Llama-3-8B cascade step, B=64, prefix 4096)"
 FLUSH_BYTES = 256 * 1024 * 1024
-DECODE_TRAFFIC_BYTES = 162_838_528 + 4_104_960   # ncu dram__bytes_read.sum + dram__bytes_write.sum
+DECODE_TRAFFIC_BYTES = 162_836_224 + 4_373_760   # ncu dram__bytes_read.sum + dram__bytes_write.sum
 
 
 class L2Flush:
