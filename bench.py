@@ -259,6 +259,10 @@ def run_ours(args, rank, world, local):
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
 
     gateup = gateup_sweep(flush, peaks) if not args.no_gateup else None
+    # the Llama-3-70B MLP shard of the multi-GPU config: gate_up with K=8192 and
+    # the 28672 intermediate columns split across the ranks, M=256 (per rank)
+    mlp70 = (gateup_sweep(flush, peaks, Ms=(256,), K=8192, I=28672 // world, seed=11 + rank)
+             if not args.no_gateup and 28672 % (128 * world) == 0 else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -310,18 +314,23 @@ def run_ours(args, rank, world, local):
     if gateup is not None:
         line["gateup_swiglu"] = gateup
         line["gpu_launches"] += gateup.pop("_launches")
+    if mlp70 is not None:
+        mlp70["shape"] = (f"Llama-3-70B MLP shard: X[256,8192] x W[2*{28672 // world},8192]^T -> "
+                          f"silu(gate)*up bf16 [256,{28672 // world}] per rank ({world} rank(s))")
+        line["gateup_swiglu_70b_shard"] = mlp70
+        line["gpu_launches"] += mlp70.pop("_launches")
     if cpu is not None:
         line["cpu_baseline"] = cpu
     return line
 
 
-def gateup_sweep(flush, peaks, Ms=(1, 16, 64, 256, 4096), K=4096, I=14336, reps=5):
-    """Llama-3-8B gate_up + SwiGLU: X[M,4096] x W[2*14336,4096]^T -> bf16 [M,14336]
+def gateup_sweep(flush, peaks, Ms=(1, 16, 64, 256, 4096), K=4096, I=14336, reps=5, seed=7):
+    """gate_up + SwiGLU (default: Llama-3-8B, X[M,4096] x W[2*14336,4096]^T -> bf16 [M,14336])
     through torch.ops.npu.cascade_gateup_swiglu (one tcgen05 kernel per call).
     Per M: TFLOP/s (tensor bound at M=4096) and GB/s (HBM bound for M<=256)."""
     import torch
     npu = torch.ops.npu
-    g = torch.Generator(device="cuda").manual_seed(7)
+    g = torch.Generator(device="cuda").manual_seed(seed)
     w = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     res, launches = {}, 0
     for M in Ms:
