@@ -484,7 +484,29 @@ cudaError_t launch_gateup(const GateUpLaunch& L, const void* a, const void* b, c
   // up to 256 rows: one 256-row tile per CTA shares each W tile between both
   // halves (measured: equal at K=4096, 4% faster at K=8192); beyond, the
   // overlapped-epilogue form wins (684 vs 725 us at M=4096)
-  if (L.M <= 2 * kBM) return launch_bn<128, 2>(L, a, b, stream);
+  if (L.M <= 2 * kBM) {
+    // Few rows: the weight stream is spread over as many CTAs as there are
+    // SMs. Of the tile forms (256 x 128 with a shared W tile, 128 x 128,
+    // 128 x 64), take the one with the most tiles that still fits in one
+    // wave; if none fits, the one with the fewest. Measured at M=256 (us):
+    // K=8192 I=3584 [100 / 66 / 61], I=7168 [103 / 70 / 111], I=28672
+    // [227 / 240 / 350]; K=4096 I=14336 [70 / 72 / 109].
+    int dev = 0, sms = kNumSMs;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t cand[3] = {
+        L.M > kBM && L.I % 128 == 0 ? (L.M + 2 * kBM - 1) / (2 * kBM) * (L.I / 128) : -1,
+        L.I % 128 == 0 ? (L.M + kBM - 1) / kBM * (L.I / 128) : -1,
+        L.I % 64 == 0 ? (L.M + kBM - 1) / kBM * (L.I / 64) : -1};
+    int best = -1;
+    for (int c = 0; c < 3; ++c)
+      if (cand[c] > 0 && cand[c] <= sms && (best < 0 || cand[c] > cand[best])) best = c;
+    if (best < 0)
+      for (int c = 0; c < 3; ++c)
+        if (cand[c] > 0 && (best < 0 || cand[c] < cand[best])) best = c;
+    if (best == 0) return launch_bn<128, 2>(L, a, b, stream);
+    if (best == 2) return launch_bn<64, 1>(L, a, b, stream);
+  }
   return launch_bn<128>(L, a, b, stream);
 }
 
