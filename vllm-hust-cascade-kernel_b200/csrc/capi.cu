@@ -68,7 +68,7 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens, int64_t* num_splits) {
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
   if (kernel == 0) {
-    // 256-token splits, widened (in 64-token tiles) so no request has more than kMaxSplits
+    // 512-token splits, widened (in 64-token tiles) so no request has more than kMaxSplits
     *split_tokens = std::max<int64_t>(kDecodeSplit, ceil_div(ceil_div(cap, kMaxSplits), 64) * 64);
   } else {
     const int64_t group = p->num_heads / p->kv_heads;
