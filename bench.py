@@ -264,6 +264,8 @@ def run_ours(args, rank, world, local):
     mlp70 = (gateup_sweep(flush, peaks, Ms=(256,), K=8192, I=28672 // world, seed=11 + rank)
              if not args.no_gateup and 28672 % (128 * world) == 0 else None)
 
+    verify = verify_sharded(args, rank, world, graph.replay()) if world > 1 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, args.cpu_threads)
@@ -321,7 +323,51 @@ def run_ours(args, rank, world, local):
         line["gpu_launches"] += mlp70.pop("_launches")
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if verify is not None:
+        line["verify"] = verify
     return line
+
+
+def verify_sharded(args, rank, world, out_local):
+    """After timing: reassemble the sharded outputs with NCCL all_gather (the
+    only collective on the data) and check them on rank 0 against a single-GPU
+    run of every rank's shard -- the attention step output [T, H, D] of each
+    rank's kv-head shard, and the gate_up + SwiGLU output [M, I/N] of each
+    rank's column shard of the 70B MLP (X replicated, W rows split)."""
+    import torch
+    import torch.distributed as dist
+    from cascade_kernel import workloads
+    from cascade_kernel.cascade import cascade_decode
+    res = {"collective": "torch.distributed.all_gather_into_tensor (NCCL)", "ranks": world}
+    g_att = torch.empty((world,) + tuple(out_local.shape), dtype=out_local.dtype, device="cuda")
+    dist.all_gather_into_tensor(g_att, out_local.contiguous())
+    # gate_up column shard: X[256, 8192] shared, W shard [2 * 28672/N, 8192] per rank
+    I_r = 28672 // world
+    def mlp_inputs(r):
+        gx = torch.Generator(device="cuda").manual_seed(99)
+        x = torch.randn(256, 8192, device="cuda", generator=gx).to(torch.bfloat16)
+        gw = torch.Generator(device="cuda").manual_seed(500 + r)
+        w = (torch.randn(2 * I_r, 8192, device="cuda", generator=gw) * 0.02).to(torch.bfloat16)
+        return x, w
+    x, w = mlp_inputs(rank)
+    mlp_local = torch.ops.npu.cascade_gateup_swiglu(x, w)
+    del x, w
+    g_mlp = torch.empty((world,) + tuple(mlp_local.shape), dtype=mlp_local.dtype, device="cuda")
+    dist.all_gather_into_tensor(g_mlp, mlp_local.contiguous())
+    torch.cuda.synchronize()
+    if rank == 0:
+        att_ok, mlp_ok = True, True
+        for r in range(world):
+            wr = workloads.c2_llama8b(seed=args.seed + 1000 * r)
+            att_ok &= bool(torch.equal(g_att[r], cascade_decode(wr.q, wr.k_pool, wr.v_pool, wr.tables)))
+            del wr
+            x, w = mlp_inputs(r)
+            mlp_ok &= bool(torch.equal(g_mlp[r], torch.ops.npu.cascade_gateup_swiglu(x, w)))
+            del x, w
+        res["attention_equal_to_single_gpu"] = att_ok
+        res["gateup_equal_to_single_gpu"] = mlp_ok
+    dist.barrier()
+    return res
 
 
 def gateup_sweep(flush, peaks, Ms=(1, 16, 64, 256, 4096), K=4096, I=14336, reps=5, seed=7):
