@@ -165,3 +165,23 @@ def test_step_graph_replay_with_host_io():
         io.replay()
         torch.cuda.synchronize()
         assert torch.equal(out_h, cascade_decode(q_new, w.k_pool, w.v_pool, t).cpu())
+
+
+def test_vllm_kv_cache_layout_views():
+    """vLLM keeps K and V in one tensor [2, numBlocks, blockSize, KVH, D]; its
+    kv_cache[0] / kv_cache[1] are contiguous [numBlocks, blockSize, KVH, D]
+    views, which the ops take as the K and V pools without a copy."""
+    import torch
+    from cascade_kernel.cascade import cascade_decode
+    Hh.need_cuda()
+    kw = dict(CASES["c2_like_b16"])
+    kw["dtype"] = torch.bfloat16
+    w = _work("vllm_layout", **kw)
+    kv_cache = torch.stack([w.k_pool, w.v_pool])           # [2, NB, bs, KVH, D]
+    k_view, v_view = kv_cache[0], kv_cache[1]
+    assert k_view.is_contiguous() and v_view.is_contiguous()
+    assert k_view.data_ptr() == kv_cache.data_ptr()        # a view, no copy
+    a = cascade_decode(w.q, w.k_pool, w.v_pool, w.tables)
+    b = cascade_decode(w.q, k_view, v_view, w.tables)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
