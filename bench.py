@@ -11,16 +11,20 @@ pages, per-request suffix decode, LSE merge to the bf16 output.
 
 Multi-GPU (torchrun, one rank per GPU): attention is partitioned by kv head
 with no hot-path collective, so every rank owns 8 kv heads / 32 q heads of a
-model with 8N kv heads (weak scaling); NCCL is used only for the barrier and
-the max-over-ranks timing.
+model with 8N kv heads (weak scaling); NCCL is used only for the barrier, the
+max-over-ranks timing and, after timing, the all_gather of the sharded
+outputs that rank 0 checks against single-GPU runs.
 
-``value`` = algorithmic bytes of all ranks / max-over-ranks device time.
-L2 is flushed before every timed step -- a 256 MiB write, then a 256 MiB read
-of a second buffer so the write's dirty lines are written back before the
-step starts instead of stealing DRAM bandwidth from it; each step is timed
-with CUDA events on the launching stream.  ``e2e`` repeats the step through
-the public op with host buffers: q and the tables copied from pinned host
-memory and the output copied back inside the timed region.
+``value`` = algorithmic bytes of all ranks / max-over-ranks device time of
+exactly K steps.  The K timed steps are captured back to back in one CUDA
+graph, as a decode forward runs attention layer after layer; step i reads
+layer (i mod 8)'s own q and K/V pools (8 x 185 MB, far more than the 126 MB
+L2), so consecutive steps never find their K/V in L2.  The same step timed
+alone (L2 flushed by a 256 MiB write and a 256 MiB read before it, one event
+pair around a one-step graph) is reported beside it.  ``e2e`` repeats the K
+steps through the public API with host buffers: every step's q and tables
+are copied from pinned host memory and its output copied back inside the
+timed graph.
 ``--impl reference`` times the reference's CPU golden path (its numpy fp64
 restatement in oracle/) on the host cores, on rank 0 only.
 """
@@ -37,6 +41,8 @@ sys.path.insert(0, os.path.join(ROOT, "vllm-hust-cascade-kernel_b200"))
 
 METRIC = "cascade decode attention HBM GB/s (Llama-3-8B cascade step, B=64, prefix 4096)"
 FLUSH_BYTES = 256 * 1024 * 1024
+LAYERS = 8          # distinct per-layer q/K/V sets the timed steps rotate through
+STEP_KERNELS = 3    # suffix decode + stage-1 + combine
 DECODE_TRAFFIC_BYTES = 162_836_224 + 4_373_760   # ncu dram__bytes_read.sum + dram__bytes_write.sum
 
 
@@ -152,106 +158,144 @@ def run_ours(args, rank, world, local):
     import torch
     import cascade_kernel  # noqa: F401  (registers the ops; fails loudly if unbuilt)
     from cascade_kernel import capi, workloads
-    from cascade_kernel.cascade import cascade_decode
+    from cascade_kernel.cascade import CascadeLayersGraph, CascadeStepGraph, cascade_decode
 
-    npu = torch.ops.npu
     peaks = _peaks()
     w = workloads.c2_llama8b(seed=args.seed + 1000 * rank)
     t = w.tables
     stream = torch.cuda.current_stream()
-    flush = L2Flush(torch)
     ab = w.algorithmic_bytes()
 
-    # the step is captured once in a CUDA graph (three kernels, no host work
-    # per replay), as a serving loop runs it
-    from cascade_kernel.cascade import CascadeStepGraph
-    graph = CascadeStepGraph(w.q, w.k_pool, w.v_pool, t)
-    eager_ref = cascade_decode(w.q, w.k_pool, w.v_pool, t)
-    torch.cuda.synchronize()
-    assert torch.equal(graph.replay(), eager_ref), "graph replay differs from the eager step"
+    # Per-layer inputs, as a decode forward walks the layers: layer 0 is the
+    # workload's own q/K/V, layers 1.. are seeded N(0,1) tensors of the same
+    # shapes; all layers share the tables. The timed steps rotate through the
+    # layers, so consecutive steps read different K/V (LAYERS x 185 MB, far
+    # more than the 126 MB L2): no L2 flush is needed between them.
+    layers = [(w.q, w.k_pool, w.v_pool)]
+    for l in range(1, LAYERS):
+        gen = torch.Generator(device="cuda").manual_seed(7919 * (args.seed + 1) + 1000 * rank + l)
+        layers.append(tuple(torch.randn(x.shape, device="cuda", generator=gen).to(x.dtype)
+                            for x in (w.q, w.k_pool, w.v_pool)))
+    K = args.steps
+    lay = [i % LAYERS for i in range(K)]
 
-    def step():
-        return graph.replay()
+    # the K timed steps are captured in ONE CUDA graph (3 kernels per step, no
+    # host work), as a serving loop replays a decode forward
+    graph = CascadeLayersGraph([layers[l] + (t,) for l in lay])
+    outs = graph.replay()
+    torch.cuda.synchronize()
+    for i in range(min(K, LAYERS)):
+        assert torch.equal(outs[i], cascade_decode(*layers[lay[i]], t)), "graph step differs from the eager step"
 
     # the dominant kernel alone: the suffix decode kernel writing its split
-    # partials (C ABI, CASCADE_FLAG_PARTIALS_ONLY: one launch, no combine)
-    dom_desc = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens,
-                               t.suffix_kv_seqlens, 1, flags=capi.FLAG_PARTIALS_ONLY)
-    dom_ws = torch.empty(capi.suffix_workspace_size(dom_desc), dtype=torch.uint8, device="cuda")
+    # partials (C ABI, CASCADE_FLAG_PARTIALS_ONLY: one launch, no combine),
+    # K launches rotating through the layers' pools
+    dom_desc = [capi.paged_desc(q, k, v, t.suffix_block_table, t.suffix_q_seqlens, t.suffix_kv_seqlens, 1,
+                                flags=capi.FLAG_PARTIALS_ONLY) for q, k, v in layers]
+    dom_ws = torch.empty(capi.suffix_workspace_size(dom_desc[0]), dtype=torch.uint8, device="cuda")
 
-    def suffix_op():
-        capi.suffix_decode(dom_desc, None, None, dom_ws)
+    def suffix_ops():
+        for l in lay:
+            capi.suffix_decode(dom_desc[l], None, None, dom_ws)
 
-    # one step = stage-1 kernel + suffix decode kernel + the step combine
-    def n_launches():
-        return 3
+    suffix_ops()
+    torch.cuda.synchronize()
+    dom_graph = torch.cuda.CUDAGraph()       # the K launches back to back, no host gaps
+    with torch.cuda.graph(dom_graph):
+        suffix_ops()
 
-    for _ in range(args.warmup):
-        step()
+    def burn(seconds):
+        # back-to-back replays outside the timed regions, so that the clock
+        # samples are taken under the step's own load
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end:
+            for _ in range(8):
+                graph.replay()
+            torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        cascade_decode(*layers[i % LAYERS], t)
+        capi.suffix_decode(dom_desc[i % LAYERS], None, None, dom_ws)
+    graph.replay()
     torch.cuda.synchronize()
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            flush()
-            e0, e1, e2, e3 = ev[i]
-            e0.record(stream)
-            step()
-            e1.record(stream)
-            flush()
-            e2.record(stream)
-            suffix_op()          # the dominant kernel, timed on its own stream position
-            e3.record(stream)
+        burn(0.4)
+        barrier(world)
         torch.cuda.synchronize()
+        ev[0].record(stream)
+        graph.replay()                      # exactly K steps
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ev[2].record(stream)
+        dom_graph.replay()                  # K launches of the dominant kernel
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        burn(0.2)
     barrier(world)
-    step_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
-    dom_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
-    step_ms = max_over_ranks(step_ms, world)
-    dom_ms = max_over_ranks(dom_ms, world)
+    step_ms = max_over_ranks(ev[0].elapsed_time(ev[1]) / K, world)
+    dom_ms = max_over_ranks(ev[2].elapsed_time(ev[3]) / K, world)
 
-    # e2e through the public API with host buffers: every step copies its inputs
-    # (q and the six index tensors, packed into one pinned host buffer -> one
-    # H2D copy) and reads the merged output back (one D2H copy)
+    # the same step timed alone: L2 flushed before each step, one event pair
+    # around a one-step graph (reported beside the rotating-layer number)
+    flush = L2Flush(torch)
+    one = CascadeStepGraph(w.q, w.k_pool, w.v_pool, t)
+    fev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    torch.cuda.synchronize()
+    for a, b in fev:
+        flush()
+        a.record(stream)
+        one.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    flushed_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in fev) / K, world)
+    del one
+
+    # e2e through the public API with host buffers: every step copies its
+    # layer's inputs (q and the six index tensors, packed into one pinned
+    # host buffer -> one H2D copy) and reads its merged output back (one D2H
+    # copy), all inside the K-step graph (CascadeLayersGraph with host_io)
     tabs = [t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens, t.suffix_block_table,
             t.suffix_q_seqlens, t.suffix_kv_seqlens]
-    parts = [w.q] + tabs
-    offs, cur = [], 0
-    for x in parts:
-        offs.append(cur)
-        cur += (x.numel() * x.element_size() + 255) // 256 * 256
-    host_in = torch.empty(cur, dtype=torch.uint8).pin_memory()
-    for x, o in zip(parts, offs):
-        nb = x.numel() * x.element_size()
-        host_in[o:o + nb].copy_(x.contiguous().view(-1).view(torch.uint8).cpu())
-    dev_in = torch.empty(cur, dtype=torch.uint8, device="cuda")
-    views = [dev_in[o:o + x.numel() * x.element_size()].view(x.dtype).view(x.shape) for x, o in zip(parts, offs)]
-    out_h = torch.empty(w.q.shape, dtype=torch.bfloat16).pin_memory()
     from cascade_kernel.cascade import CascadeTables
-    tt = CascadeTables(*views[1:], uniform_group=t.uniform_group)
-    dev_in.copy_(host_in)
-    # one graph per step: the H2D copy of this step's q + index tensors, the
-    # three kernels, the D2H copy of the merged output
-    e2e_graph = CascadeStepGraph(views[0], w.k_pool, w.v_pool, tt, host_io=(host_in, dev_in, out_h))
-
-    def e2e_step():
-        e2e_graph.replay()
-
-    for _ in range(max(3, args.warmup)):
-        e2e_step()
+    io, e2e_in = [], []
+    for q, k, v in layers:
+        parts = [q] + tabs
+        offs, cur = [], 0
+        for x in parts:
+            offs.append(cur)
+            cur += (x.numel() * x.element_size() + 255) // 256 * 256
+        host_in = torch.empty(cur, dtype=torch.uint8).pin_memory()
+        for x, o in zip(parts, offs):
+            nb = x.numel() * x.element_size()
+            host_in[o:o + nb].copy_(x.contiguous().view(-1).view(torch.uint8).cpu())
+        dev_in = torch.empty(cur, dtype=torch.uint8, device="cuda")
+        dev_in.copy_(host_in)
+        views = [dev_in[o:o + x.numel() * x.element_size()].view(x.dtype).view(x.shape)
+                 for x, o in zip(parts, offs)]
+        out_h = torch.empty(q.shape, dtype=torch.bfloat16).pin_memory()
+        io.append((host_in, dev_in, out_h))
+        e2e_in.append((views[0], k, v, CascadeTables(*views[1:], uniform_group=t.uniform_group)))
+    # the copies run on copy streams inside the graph: step i's inputs load
+    # while earlier steps compute, its output drains while later ones do
+    e2e_graph = CascadeLayersGraph([e2e_in[l] for l in lay], host_io=[io[l] for l in lay], overlap_io=True)
+    e2e_graph.replay()
     torch.cuda.synchronize()
-    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    assert torch.equal(io[lay[-1]][2], outs[K - 1].cpu()), "e2e output differs from the device-resident step"
+    e2e_ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     barrier(world)
-    for i in range(args.steps):
-        flush()
-        e2e_ev[i][0].record(stream)
-        e2e_step()
-        e2e_ev[i][1].record(stream)
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_ev) / args.steps, world)
-    h2d = cur
-    d2h = out_h.numel() * out_h.element_size()
+    e2e_ev[0].record(stream)
+    e2e_graph.replay()                      # exactly K steps, host copies included
+    e2e_ev[1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e2e_ev[0].elapsed_time(e2e_ev[1]) / K, world)
+    h2d = io[0][0].numel()
+    d2h = io[0][2].numel() * io[0][2].element_size()
+    del e2e_graph, io, e2e_in, dom_graph
 
     total_bytes = ab["total"] * world
     value = total_bytes / (step_ms * 1e-3) / 1e9
@@ -264,7 +308,8 @@ def run_ours(args, rank, world, local):
     mlp70 = (gateup_sweep(flush, peaks, Ms=(256,), K=8192, I=28672 // world, seed=11 + rank)
              if not args.no_gateup and 28672 % (128 * world) == 0 else None)
 
-    verify = verify_sharded(args, rank, world, graph.replay()) if world > 1 else None
+    verify = verify_sharded(args, rank, world, outs[0]) if world > 1 else None
+    del graph
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -290,11 +335,18 @@ def run_ours(args, rank, world, local):
             "suffix_tokens": int(w.suffix_lens.sum()),
             "algorithmic_bytes_per_step_per_rank": ab,
             "parallelism": f"kv-head partition x{world} (weak: 8 kv heads per rank)",
-            "l2": "flushed before every timed step (256 MiB write, then 256 MiB read of another buffer)",
-            "launch": "step captured in a CUDA graph (CascadeStepGraph), replayed per step",
+            "l2": (f"inputs larger than L2: the K timed steps rotate through {LAYERS} layers' q/K/V "
+                   f"({LAYERS} x {ab['total'] / 1e6:.0f} MB vs 126 MB L2), so no step re-reads cached K/V"),
+            "launch": "the K timed steps captured back to back in one CUDA graph (CascadeLayersGraph), "
+                      "one replay, as a decode forward runs its layers",
+            "layers": LAYERS,
         },
+        # the same step timed alone: L2 flushed (256 MiB write + 256 MiB read)
+        # before each step and one event pair around a one-step graph replay
+        "us_per_step_flushed_alone": round(flushed_ms * 1e3, 2),
         "roofline": {
-            "kernel": "paged_decode_kernel (suffix decode, split partials; one launch)",
+            "kernel": "paged_decode_kernel (suffix decode, split partials; K launches rotating through "
+                      "the layers' pools, average launch duration)",
             "bound": "hbm",
             "achieved": round(achieved, 1),
             "peak": peaks["hbm_gbs"],
@@ -308,9 +360,12 @@ def run_ours(args, rank, world, local):
         },
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "us_per_step": round(e2e_ms * 1e3, 2), "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h)},
-        # step (graph replay), the dominant kernel alone, and the e2e step (graph replay)
-        "gpu_launches": 2 * n_launches() * args.steps + args.steps,
+                "d2h_bytes_per_step": int(d2h),
+                "how": "K steps in one graph, each copying its q + tables in from pinned host memory and its "
+                       "output out; copies on copy streams overlap neighbouring steps' kernels"},
+        # timed regions: the K-step graph, K dominant-kernel launches, the
+        # flushed one-step replays and the K-step e2e graph
+        "gpu_launches": 3 * STEP_KERNELS * K + K,
         "clocks": clk.summary(),
     }
     line["frac_of_hbm_roofline_step"] = round(value / world / peaks["hbm_gbs"], 4)

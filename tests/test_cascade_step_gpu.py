@@ -185,3 +185,81 @@ def test_vllm_kv_cache_layout_views():
     b = cascade_decode(w.q, k_view, v_view, w.tables)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+def test_layers_graph_steps_and_host_io():
+    """CascadeLayersGraph: several steps, each on its own layer's q/K/V, in
+    one graph. Every step's output equals the eager step on that layer, and
+    with per-step host_io each step's pinned host output is its own result."""
+    import torch
+    from cascade_kernel.cascade import CascadeLayersGraph, CascadeTables, cascade_decode
+    Hh.need_cuda()
+    kw = dict(CASES["c1_like"])
+    kw["dtype"] = torch.float16
+    kw["group_sizes"], kw["suffix_lens"] = [4, 4], [64, 100, 200, 256, 0, 17, 128, 300]
+    kw["prefix_lens"] = [512, 384]
+    w = _work("layers", **kw)
+    t = w.tables
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    layers = [(w.q, w.k_pool, w.v_pool)] + [
+        tuple(torch.randn(x.shape, device="cuda", generator=gen).to(x.dtype) for x in (w.q, w.k_pool, w.v_pool))
+        for _ in range(2)]
+    order = [0, 1, 2, 1]
+    g = CascadeLayersGraph([layers[l] + (t,) for l in order])
+    outs = g.replay()
+    torch.cuda.synchronize()
+    assert len(outs) == len(order)
+    for o, l in zip(outs, order):
+        assert torch.equal(o, cascade_decode(*layers[l], t))
+    # per-step host io: the query of each step comes from its own pinned buffer
+    ios, steps = [], []
+    for l in order:
+        q = layers[l][0]
+        host_in = torch.empty(q.numel() * q.element_size(), dtype=torch.uint8).pin_memory()
+        host_in.copy_(q.contiguous().view(-1).view(torch.uint8).cpu())
+        dev_in = torch.empty_like(host_in, device="cuda")
+        qv = dev_in.view(q.dtype).view(q.shape)
+        out_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        ios.append((host_in, dev_in, out_h))
+        steps.append((qv, layers[l][1], layers[l][2], t))
+    gi = CascadeLayersGraph(steps, host_io=ios)
+    gi.replay()
+    torch.cuda.synchronize()
+    for (_, _, out_h), l in zip(ios, order):
+        assert torch.equal(out_h, cascade_decode(*layers[l], t).cpu())
+    with pytest.raises(ValueError):
+        CascadeLayersGraph(steps, host_io=ios[:1])
+
+
+def test_layers_graph_overlapped_host_io_reuses_buffers_safely():
+    """overlap_io=True where steps share device input buffers (steps 0 and 2
+    load different host queries into the same dev_in, as do 1 and 3): step 2's
+    host->device copy must wait until step 0 has read the buffer, so every
+    step's pinned output equals the eager step on its OWN query."""
+    import torch
+    from cascade_kernel.cascade import CascadeLayersGraph, cascade_decode
+    Hh.need_cuda()
+    kw = dict(CASES["c1_like"])
+    kw["dtype"] = torch.float16
+    w = _work("layers_ovl", **kw)
+    t = w.tables
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    k2, v2 = (torch.randn(x.shape, device="cuda", generator=gen).to(x.dtype) for x in (w.k_pool, w.v_pool))
+    pools = [(w.k_pool, w.v_pool), (k2, v2), (k2, v2), (w.k_pool, w.v_pool)]
+    nbytes = w.q.numel() * w.q.element_size()
+    dins = [torch.empty(nbytes, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    use = [0, 1, 0, 1]
+    qs = [torch.randn(w.q.shape, device="cuda", generator=gen).to(w.q.dtype) for _ in use]
+    steps, io = [], []
+    for i, b in enumerate(use):
+        hin = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        hin.copy_(qs[i].view(-1).view(torch.uint8).cpu())
+        out_h = torch.empty(w.q.shape, dtype=w.q.dtype).pin_memory()
+        steps.append((dins[b].view(w.q.dtype).view(w.q.shape), pools[i][0], pools[i][1], t))
+        io.append((hin, dins[b], out_h))
+    g = CascadeLayersGraph(steps, host_io=io, overlap_io=True)
+    for _ in range(2):
+        g.replay()
+        torch.cuda.synchronize()
+        for i in range(len(use)):
+            assert torch.equal(io[i][2], cascade_decode(qs[i], pools[i][0], pools[i][1], t).cpu())

@@ -67,16 +67,108 @@ def cascade_decode(q, k_pool, v_pool, tables: CascadeTables, out_dtype=None, fus
     return npu.cascade_lse_merge(o1, o2, l1, l2, code)
 
 
-class CascadeStepGraph:
-    """A cascade decode step captured once in a CUDA graph and replayed.
+class CascadeLayersGraph:
+    """Several cascade decode steps captured back to back in ONE CUDA graph,
+    as a decode forward runs attention layer after layer: step i reads its
+    own query and K/V pools ``steps[i] = (q, k_pool, v_pool, tables)``.
 
-    The step's inputs live in fixed device buffers (``q``, the pools and the
-    ``tables`` given at construction); a serving loop writes the next step's
-    queries and index tensors into them in place and calls ``replay()``,
-    which re-issues the suffix, stage-1 and combine kernels without any host
-    work. Requires the uniform-q path (``tables.uniform_group > 0``): the
+    ``replay()`` re-issues every step's suffix, stage-1 and combine kernels
+    with no host work and returns the list of step outputs (fixed device
+    tensors, overwritten by every replay). A serving loop writes the next
+    step's queries and index tensors into the captured buffers in place.
+    Requires the uniform-q path (``tables.uniform_group > 0``): the
     per-request path reads seqlens back to the host and cannot be captured.
 
+    ``host_io`` (optional, one ``(host_in, dev_in, host_out)`` triple per
+    step) puts each step's host traffic in the graph: before step i the
+    pinned host buffer ``host_in`` is copied into the device buffer
+    ``dev_in`` (which must back that step's q and tables), and after it the
+    step's output is copied into the pinned host tensor ``host_out``.
+
+    ``overlap_io=True`` issues those copies on two copy streams inside the
+    graph instead of in line with the kernels: step i's host->device copy
+    waits only for the last earlier step that reads the same ``dev_in`` (so
+    it can run while the steps before it compute), step i's kernels wait for
+    that copy, and step i's device->host copy waits only for step i. Every
+    step still moves its own inputs in and its own output out.
+    """
+
+    def __init__(self, steps, out_dtype=None, warmup=2, host_io=None, overlap_io=False):
+        steps = list(steps)
+        if not steps:
+            raise ValueError("CascadeLayersGraph needs at least one step")
+        for st in steps:
+            if st[3].uniform_group <= 0:
+                raise ValueError("CascadeLayersGraph needs uniform prefix groups (tables.uniform_group > 0)")
+        if host_io is not None and len(host_io) != len(steps):
+            raise ValueError("host_io needs one (host_in, dev_in, host_out) triple per step")
+        self.steps, self.out_dtype, self.host_io = steps, out_dtype, host_io
+        io_streams = (torch.cuda.Stream(), torch.cuda.Stream()) if host_io is not None and overlap_io else None
+
+        def run_overlapped():
+            main = torch.cuda.current_stream()
+            s_in, s_out = io_streams
+            s_in.wait_stream(main)
+            s_out.wait_stream(main)
+            outs, done, last_use = [], [], {}
+            for i, (q, k_pool, v_pool, tables) in enumerate(steps):
+                host_in, dev_in, host_out = host_io[i]
+                with torch.cuda.stream(s_in):
+                    j = last_use.get(dev_in.data_ptr())
+                    if j is not None:
+                        s_in.wait_event(done[j])
+                    dev_in.copy_(host_in, non_blocking=True)
+                    loaded = torch.cuda.Event()
+                    loaded.record(s_in)
+                main.wait_event(loaded)
+                out = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+                fin = torch.cuda.Event()
+                fin.record(main)
+                done.append(fin)
+                last_use[dev_in.data_ptr()] = i
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(fin)
+                    host_out.copy_(out, non_blocking=True)
+                outs.append(out)
+            main.wait_stream(s_in)
+            main.wait_stream(s_out)
+            return outs
+
+        def run():
+            if io_streams is not None:
+                return run_overlapped()
+            outs = []
+            for i, (q, k_pool, v_pool, tables) in enumerate(steps):
+                io = None if host_io is None else host_io[i]
+                if io is not None:
+                    io[1].copy_(io[0], non_blocking=True)
+                out = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+                if io is not None:
+                    io[2].copy_(out, non_blocking=True)
+                outs.append(out)
+            return outs
+
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                run()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.outs = run()
+
+    def replay(self):
+        self.graph.replay()
+        return self.outs
+
+
+class CascadeStepGraph(CascadeLayersGraph):
+    """One cascade decode step captured in a CUDA graph and replayed (a
+    one-step ``CascadeLayersGraph``).
+
+    The step's inputs live in fixed device buffers (``q``, the pools and the
+    ``tables`` given at construction); ``replay()`` returns the output.
     ``host_io=(host_in, dev_in, host_out)`` puts the step's host traffic in
     the same graph: every replay first copies the pinned host buffer
     ``host_in`` into the device buffer ``dev_in`` (which must back ``q`` and
@@ -88,26 +180,9 @@ class CascadeStepGraph:
         if tables.uniform_group <= 0:
             raise ValueError("CascadeStepGraph needs uniform prefix groups (tables.uniform_group > 0)")
         self.q, self.k_pool, self.v_pool, self.tables = q, k_pool, v_pool, tables
-        self.out_dtype = out_dtype
-        self.host_io = host_io
-
-        def step():
-            if host_io is not None:
-                host_io[1].copy_(host_io[0], non_blocking=True)
-            out = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
-            if host_io is not None:
-                host_io[2].copy_(out, non_blocking=True)
-            return out
-
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(warmup):
-                step()
-        torch.cuda.current_stream().wait_stream(side)
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self.out = step()
+        super().__init__([(q, k_pool, v_pool, tables)], out_dtype, warmup,
+                         None if host_io is None else [host_io])
+        self.out = self.outs[0]
 
     def replay(self):
         self.graph.replay()
