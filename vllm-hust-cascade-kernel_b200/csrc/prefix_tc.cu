@@ -7,26 +7,30 @@
 // QK^T / PV contraction (the shared-prefix stage of the reference,
 // ascend-kernel/csrc/ops/fa_fp32_stage1/op_kernel/kernel_fa_fp32_stage1.cpp:143-745).
 //
-// One CTA = (KV split, kv head x 128-row tile, request); 10 warps:
-//   warp 8    TMA producer: 128-token K and V tiles gathered page by page
-//             through block_table (2-D boxes [min(bs,128) rows x 64 dims],
-//             128-byte swizzle), double-buffered;
+// One CTA = (KV split, kv head x 128-row tile, request); 11 warps:
+//   warp 8    K producer, warp 10 V producer: 128-token K and V tiles gathered
+//             page by page through block_table (2-D boxes [min(bs,128) rows x
+//             64 dims], 128-byte swizzle) into two 3-stage rings. Two issuing
+//             threads: one thread's TMA issue rate caps a CTA near 76 GB/s;
 //   warp 9    MMA issuer (one thread): S_j = Q K_j^T (M=N=K=128) into a TMEM S
-//             buffer; O += P_j V_j into the TMEM O accumulator;
+//             buffer and O += P_j V_j into the TMEM O accumulator, both with
+//             the A operand (Q, P) read from tensor memory;
 //   warps 0-3 softmax: thread i owns query row i == TMEM lane i. One
 //             tcgen05.ld of the 128-column S row, running max and
 //             unquantised row sum, P = round16(exp(S - m)) (RNE: the
 //             reference's quantisation point,
-//             block_epilogue_online_softmax_no_mask.hpp:578-591) into swizzled
-//             smem as the A operand of PV;
-//   warps 4-7 correction + epilogue: before P_j V_j is accumulated, the TMEM
-//             accumulator is rescaled O = dm_j * O (the reference's rescale,
+//             block_epilogue_online_softmax_no_mask.hpp:578-591) written back
+//             over the first 64 columns of the same S buffer (two 16-bit
+//             values per column) as the A operand of PV;
+//   warps 4-7 correction + epilogue: they load Q into tensor memory, and
+//             before P_j V_j is accumulated they rescale the TMEM accumulator
+//             O = dm_j * O (the reference's rescale,
 //             block_epilogue_rescale_o_no_split_row.hpp:144-268) -- skipped,
 //             exactly, for a warp whose 32 rows all kept their max (dm == 1);
-//             they also load Q and write the final O / l and LSE.
-// TMEM: S[2] at columns 0/128, O at 256. Shared memory: Q 32 KB, K 2x32 KB,
-// V 2x32 KB, P 32 KB. LSE = ln(l) + m (natural log), written 8x per row
-// (stage-1 padded layout) or as a split partial for a later combine.
+//             at the end they write O / l and the LSE.
+// TMEM: S[2] at columns 0/128 (P_j aliases S_j), O at 256, Q at 384. Shared
+// memory: K 3x32 KB, V 3x32 KB. LSE = ln(l) + m (natural log), written 8x per
+// row (stage-1 padded layout) or as a split partial for a later combine.
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -35,32 +39,40 @@ namespace {
 
 constexpr int kRows = 128;
 constexpr int kTok = 128;
-constexpr int kThreads = 10 * 32;
-constexpr int kProducerWarp = 8;
+constexpr int kThreads = 11 * 32;
+constexpr int kKProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kVProducerWarp = 10;
+constexpr int kStages = 3;              // K and V ring depth
 constexpr int kHalf = 16384;            // [128 rows][64 x 16-bit] swizzled region
 constexpr int kTileBytes = 2 * kHalf;   // [128 rows][128 x 16-bit]
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;
-constexpr int kOffV = kOffK + 2 * kTileBytes;
-constexpr int kOffP = kOffV + 2 * kTileBytes;
-constexpr int kOffAux = kOffP + kTileBytes;   // dm[2][128], l[128], m[128], barriers
+constexpr int kOffK = 0;
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffAux = kOffV + kStages * kTileBytes;   // dm[2][128], l[128], m[128], block table, barriers
 constexpr int kBtCache = 256;                 // block-table entries of one split kept in smem
 constexpr int kOffBars = kOffAux + 4 * 128 * 4 + kBtCache * 4;
 static_assert(kOffBars % 16 == 0, "mbarriers need 8-byte alignment");
 constexpr int kSmemBytes = kOffBars + 256 + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
+constexpr uint32_t kColQ = 384;         // Q as 64 columns of 16-bit pairs
 
+// Phase rules (each barrier is waited in tile order and can never complete
+// two phases ahead of its waiter):
+//   s_full[j&1]   S_j complete (commit)                  -> softmax
+//   p_full[j&1]   P_j written to TMEM (128 softmax rows)  -> MMA, before PV_j
+//   corr_go[j&1]  tile j's row maxima known (128 softmax rows) AND PV_{j-1}
+//                 complete (commit; a plain arrive for j = 0) -> correction
+//   o_ready[j&1]  O rescaled for tile j (128 rows)        -> MMA, before PV_j
 struct __align__(8) PrefixBars {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_free[2];
-  uint64_t p_full, p_free;
-  uint64_t stat_full[2], o_ready[2];
+  uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2], p_full[2], corr_go[2], o_ready[2];
   uint64_t o_final, fin;
   uint32_t tmem_base;
 };
+static_assert(sizeof(PrefixBars) <= 256, "barrier block");
 
 __device__ __forceinline__ int token_offset(const PagedAttnLaunch& p, int b) {
   if (p.q_seqlen_value > 0) return b * p.q_seqlen_value;
@@ -81,6 +93,15 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
       "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 
@@ -166,20 +187,31 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
     return;
   }
 
+  // The split's block-table entries -> smem (warp 8, one round trip) before
+  // the CTA barrier, so both producers see them.
+  const int bs = p.block_size;
+  const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
+  const int npages = (kv + bs - 1) / bs;
+  const int first_page = s_begin / bs;
+  const int nbt = min(npages, (s_end + bs - 1) / bs) - first_page;
+  const bool cached = nbt <= kBtCache;
+  if (warp == kKProducerWarp && cached) {
+    for (int i = lane; i < nbt; i += 32) btc[i] = bt[first_page + i];
+  }
   if (tid == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_free[s], 128);
-      mbar_init(&bars->stat_full[s], 128);
+      mbar_init(&bars->p_full[s], 128);
+      mbar_init(&bars->corr_go[s], 129);
       mbar_init(&bars->o_ready[s], 128);
     }
-    mbar_init(&bars->p_full, 128);
-    mbar_init(&bars->p_free, 1);
     mbar_init(&bars->o_final, 1);
     mbar_init(&bars->fin, 128);
     fence_mbar_init();
@@ -193,44 +225,30 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
   tc_fence_after();
   const uint32_t tbase = bars->tmem_base;
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ producer
-    // the split's block-table entries -> smem first (one round trip for the
-    // warp instead of a dependent load per tile)
-    const int bs = p.block_size;
-    const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
-    const int npages = (kv + bs - 1) / bs;
-    const int first_page = s_begin / bs;
-    const int nbt = min(npages, (s_end + bs - 1) / bs) - first_page;
-    const bool cached = nbt <= kBtCache;
-    if (cached) {
-      for (int i = lane; i < nbt; i += 32) btc[i] = bt[first_page + i];
-    }
-    __syncwarp();
+  if (warp == kKProducerWarp || warp == kVProducerWarp) {
+    // ---------------------------------------------------- K / V producers
     if (lane == 0) {
-      tma_prefetch_desc(&p.tmap_k);
-      tma_prefetch_desc(&p.tmap_v);
+      const bool is_v = warp == kVProducerWarp;
+      const CUtensorMap* tm = is_v ? &p.tmap_v : &p.tmap_k;
+      uint64_t* full = is_v ? bars->v_full : bars->k_full;
+      uint64_t* empty = is_v ? bars->v_empty : bars->k_empty;
+      uint8_t* ring = smem + (is_v ? kOffV : kOffK);
+      tma_prefetch_desc(tm);
       const int box_rows = bs < kTok ? bs : kTok;
       const int oob_row = p.num_blocks * bs;
       const int x0 = g * kHeadDim;
       for (int j = 0; j < ntiles; ++j) {
-        const int st = j & 1, u = j >> 1;
+        const int st = j % kStages, u = j / kStages;
         const int t_tile = s_begin + j * kTok;
-        for (int kvsel = 0; kvsel < 2; ++kvsel) {
-          uint64_t* full = kvsel ? &bars->v_full[st] : &bars->k_full[st];
-          uint64_t* empty = kvsel ? &bars->v_empty[st] : &bars->k_empty[st];
-          const CUtensorMap* tm = kvsel ? &p.tmap_v : &p.tmap_k;
-          uint8_t* dst = smem + (kvsel ? kOffV : kOffK) + st * kTileBytes;
-          if (j >= 2) mbar_wait(empty, (u - 1) & 1);
-          mbar_arrive_expect_tx(full, kTileBytes);
-          for (int off = 0; off < kTok; off += box_rows) {
-            const int t = t_tile + off;
-            const int page = t / bs;
-            const int row =
-                page < npages ? (cached ? btc[page - first_page] : bt[page]) * bs + (t % bs) : oob_row;
-            tma_load_2d(dst + off * 128, tm, full, x0, row);
-            tma_load_2d(dst + kHalf + off * 128, tm, full, x0 + 64, row);
-          }
+        uint8_t* dst = ring + st * kTileBytes;
+        if (j >= kStages) mbar_wait(&empty[st], (u - 1) & 1);
+        mbar_arrive_expect_tx(&full[st], kTileBytes);
+        for (int off = 0; off < kTok; off += box_rows) {
+          const int t = t_tile + off;
+          const int page = t / bs;
+          const int row = page < npages ? (cached ? btc[page - first_page] : bt[page]) * bs + (t % bs) : oob_row;
+          tma_load_2d(dst + off * 128, tm, &full[st], x0, row);
+          tma_load_2d(dst + kHalf + off * 128, tm, &full[st], x0 + 64, row);
         }
       }
     }
@@ -240,43 +258,43 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
       constexpr uint32_t fmt = kFp16 ? 0u : 1u;
       const uint32_t idesc_s = make_idesc_f16(128, 128, fmt, 0, 0);
       const uint32_t idesc_pv = make_idesc_f16(128, 128, fmt, 0, 1);
-      const uint32_t sQ = smem_u32(smem + kOffQ);
       const uint32_t sK = smem_u32(smem + kOffK);
       const uint32_t sV = smem_u32(smem + kOffV);
-      const uint32_t sP = smem_u32(smem + kOffP);
+      mbar_arrive(&bars->corr_go[0]);  // tile 0 has no PV_{-1} to wait for
       mbar_wait(&bars->q_full, 0);
       tc_fence_after();
       for (int j = 0; j <= ntiles; ++j) {
         if (j < ntiles) {
-          const int st = j & 1, u = j >> 1;
+          // S_j overwrites S buffer j&1, whose P_{j-2} was read by PV_{j-2}:
+          // issued earlier by this thread, so it executes first.
+          const int st = j % kStages, u = j / kStages;
           mbar_wait(&bars->k_full[st], u & 1);
-          if (j >= 2) mbar_wait(&bars->s_free[st], (u - 1) & 1);
           tc_fence_after();
           const uint32_t kb = sK + st * kTileBytes;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const uint32_t koff = (k >> 2) * kHalf + (k & 3) * 32;
-            umma_f16_ss(tbase + st * 128, make_smem_desc(sQ + koff, 16, 1024, 2),
-                        make_smem_desc(kb + koff, 16, 1024, 2), idesc_s, k > 0 ? 1u : 0u);
+            umma_f16_ts(tbase + (j & 1) * 128, tbase + kColQ + k * 8, make_smem_desc(kb + koff, 16, 1024, 2),
+                        idesc_s, k > 0 ? 1u : 0u);
           }
-          umma_commit(&bars->s_full[st]);
+          umma_commit(&bars->s_full[j & 1]);
           umma_commit(&bars->k_empty[st]);
         }
         if (j >= 1) {
           const int i = j - 1;
-          const int st = i & 1, u = i >> 1;
+          const int st = i % kStages, u = i / kStages;
           mbar_wait(&bars->v_full[st], u & 1);
-          mbar_wait(&bars->p_full, i & 1);
-          mbar_wait(&bars->o_ready[st], u & 1);
+          mbar_wait(&bars->p_full[i & 1], (i >> 1) & 1);
+          mbar_wait(&bars->o_ready[i & 1], (i >> 1) & 1);
           tc_fence_after();
           const uint32_t vb = sV + st * kTileBytes;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            umma_f16_ss(tbase + kColO, make_smem_desc(sP + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024, 2),
-                        make_smem_desc(vb + k * 2048, kHalf, 1024, 2), idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ts(tbase + kColO, tbase + (i & 1) * 128 + k * 8, make_smem_desc(vb + k * 2048, kHalf, 1024, 2),
+                        idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&bars->v_empty[st]);
-          umma_commit(&bars->p_free);
+          if (i + 1 < ntiles) umma_commit(&bars->corr_go[(i + 1) & 1]);
           if (i == ntiles - 1) umma_commit(&bars->o_final);
         }
       }
@@ -285,7 +303,6 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
     // ---------------------------------------------------------------- softmax
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const float sl2 = p.scale_log2;
-    uint8_t* pbuf = smem + kOffP;
     float m = -INFINITY, l = 0.f;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1, u = j >> 1;
@@ -298,8 +315,6 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
       tmem_ld_32x32b_x32(tbase + lane_off + st * 128 + 64, s2);
       tmem_ld_32x32b_x32(tbase + lane_off + st * 128 + 96, s3);
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&bars->s_free[st]);  // S is in registers: the buffer may be overwritten
       float s[128];
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
@@ -318,24 +333,26 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
       const float m_new = fmaxf(m, mx * sl2);
       const float dm = (m == -INFINITY) ? 1.f : ex2(m - m_new);
       dmbuf[st * kRows + tid] = dm;
-      mbar_arrive(&bars->stat_full[st]);
+      mbar_arrive(&bars->corr_go[st]);
+      // P_j over the first 64 columns of S_j (already in registers), in two
+      // 32-column halves. PV_{j-2}, the last reader of this buffer,
+      // completed before S_j did.
       float rs = 0.f;
-      uint32_t pk[64];
 #pragma unroll
-      for (int e = 0; e < kTok; e += 2) {
-        const float x0 = ex2(fmaf(s[e], sl2, -m_new));      // masked: ex2(-inf) = 0
-        const float x1 = ex2(fmaf(s[e + 1], sl2, -m_new));
-        rs += x0 + x1;
-        pk[e >> 1] = pack2<kFp16>(x0, x1);
-      }
-      if (j >= 1) mbar_wait(&bars->p_free, (j - 1) & 1);  // PV_{j-1} finished reading P
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        *reinterpret_cast<uint4*>(pbuf + (c >> 3) * kHalf + sw128(tid, c & 7)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        for (int e = 0; e < 32; e += 2) {
+          const float x0 = ex2(fmaf(s[q4 * 32 + e], sl2, -m_new));      // masked: ex2(-inf) = 0
+          const float x1 = ex2(fmaf(s[q4 * 32 + e + 1], sl2, -m_new));
+          rs += x0 + x1;
+          pk[e >> 1] = pack2<kFp16>(x0, x1);
+        }
+        tmem_st_32x32b_x16(tbase + lane_off + st * 128 + q4 * 16, pk);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->p_full);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[st]);
       l = dm * l + rs;
       m = m_new;
     }
@@ -347,34 +364,34 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
     const int r = tid - 128;  // row == TMEM lane (warp % 4 selects the lane quarter)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     {
-      // Q row -> swizzled smem (K-major A operand); rows past the unit are zero
-      uint8_t* q_s = smem + kOffQ;
-      if (r < unit_rows) {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.query) +
-                                                           out_row(r) * kHeadDim);
-        uint4 v[16];
+      // Q row -> tensor memory (A operand of S = Q K^T: 64 columns of 16-bit
+      // pairs); rows past the unit are zero
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.query) +
+                                                         out_row(r < unit_rows ? r : 0) * kHeadDim);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) v[c] = __ldg(src + c);
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t qv[32];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(q_s + (c >> 3) * kHalf + sw128(r, c & 7)) = v[c];
-      } else {
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          *reinterpret_cast<uint4*>(q_s + (c >> 3) * kHalf + sw128(r, c & 7)) = make_uint4(0, 0, 0, 0);
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = r < unit_rows ? __ldg(src + hf * 8 + c) : make_uint4(0u, 0u, 0u, 0u);
+          qv[4 * c] = v.x;
+          qv[4 * c + 1] = v.y;
+          qv[4 * c + 2] = v.z;
+          qv[4 * c + 3] = v.w;
+        }
+        tmem_st_32x32b_x32(tbase + lane_off + kColQ + hf * 32, qv);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (r == 0) mbar_arrive(&bars->q_full);
     }
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1, u = j >> 1;
-      mbar_wait(&bars->stat_full[st], u & 1);
+      // tile j's dm is in smem and PV_{j-1} has completed
+      mbar_wait(&bars->corr_go[st], u & 1);
       const float dm = dmbuf[st * kRows + r];
       if (j >= 1 && __any_sync(0xffffffffu, dm != 1.f)) {
-        // O must hold P_{j-1} V_{j-1} before it is rescaled. PV MMAs complete
-        // in order and PV_{j-2} is already complete here (the softmax waited
-        // for it before writing P_{j-1}), so the parity of p_free is unambiguous.
-        mbar_wait(&bars->p_free, (j - 1) & 1);
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
