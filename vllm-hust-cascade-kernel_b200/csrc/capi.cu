@@ -68,8 +68,14 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens, int64_t* num_splits) {
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
   if (kernel == 0) {
-    // 512-token splits, widened (in 64-token tiles) so no request has more than kMaxSplits
-    *split_tokens = std::max<int64_t>(kDecodeSplit, ceil_div(ceil_div(cap, kMaxSplits), 64) * 64);
+    // 512-token splits, widened (in 64-token tiles) so no request has more than
+    // kMaxSplits. When the (request, kv head) pairs alone fill the GPU many
+    // times over, splits of 1024 (>= 2048 pairs) or 2048 tokens (>= 4096
+    // pairs): the grid's split dimension is sized by the LONGEST request, so
+    // short requests leave most of their split CTAs empty, and each empty CTA
+    // still holds a 99 KB slot while it reads its length and exits.
+    const int64_t widen = std::min<int64_t>(4, std::max<int64_t>(1, p->batch * p->kv_heads / 1024));
+    *split_tokens = std::max<int64_t>(kDecodeSplit * widen, ceil_div(ceil_div(cap, kMaxSplits), 64) * 64);
   } else {
     const int64_t group = p->num_heads / p->kv_heads;
     const int64_t mtiles = std::max<int64_t>(p->batch, ceil_div(p->num_tokens * group, 128));
