@@ -150,6 +150,23 @@ CASCADE_API int cascade_lse_merge(const void *o1, int32_t o1_dtype, const void *
 CASCADE_API int cascade_f3_gateup_epilogue(const void *a, const void *b, void *ws, void *d, int64_t d_stride, int64_t M,
                                int64_t K, int64_t I, int32_t mode, cascade_stream_t stream);
 
+/* Residual add + RMSNorm statistics, three modes over contiguous (M, K) rows.
+ * Replaces ascend_kernel::add_rms_norm_stats
+ *   (ascend-kernel/csrc/ops/add_rms_norm_stats/op_host/add_rms_norm_stats.cpp:59-150,
+ *    schema ascend-kernel/csrc/register.cpp:27-28).
+ * x1, x2, x_out, y: [M, K] in `dtype` (CASCADE_BF16 / CASCADE_FP16), row stride K,
+ * 16-byte aligned; gamma, beta: [K] in `dtype` (beta may be NULL);
+ * rstd: fp32 [ceil(M/8)*8], rows >= M are written as 0.
+ *   mode 0: x_out = round(x1 + x2), rstd = 1/sqrt(mean(x_out^2) + eps)
+ *           (x2 and x_out required; gamma, beta, y unused)
+ *   mode 1: rstd from x1, y = round(round(x1 * rstd) * gamma + beta)
+ *           (gamma and y required; x2 and x_out unused)
+ *   mode 2: rstd from round(x1 + x2) only (x2 required).
+ * Limits (as the reference): 0 < K <= 5120, K % 16 == 0, M > 0, eps > 0. */
+CASCADE_API int cascade_add_rms_norm_stats(const void *x1, const void *x2, const void *gamma, const void *beta,
+                                           void *x_out, float *rstd, void *y, int64_t M, int64_t K, int32_t dtype,
+                                           int32_t mode, float eps, cascade_stream_t stream);
+
 /* Suffix decode that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory when they run the step: a
  * host binding the C ABI without a device allocator, or a serving loop whose

@@ -9,8 +9,14 @@ It imports, unmodified, the reference's CPU goldens
     (gen_inputs, fa_fp64_ref, fa_fp64_ref_tieband)
   * ascend-kernel/csrc/ops/lse_merge/test/lse_merge_cases.py
     (make_inputs, fp64_ref, boundary_cases)
+  * ascend-kernel/csrc/ops/add_rms_norm_stats/test/add_rms_norm_stats_cases.py
+    and add_rms_norm_stats_ref.py (make_inputs, cpu_ref)
 runs them on small seeded cases and writes their inputs/outputs to
-``tests/golden/*.npz``.  The GPU box never reads the reference; the tests read
+``tests/golden/*.npz``.  It also copies, from the reference's device
+self-check record add_rms_norm_stats/test/f2_golden_selfcheck.json, the
+per-element dumps (row, col, fp64 golden, CANN's value and rstd, gamma) and
+the per-case error statistics into
+``tests/golden/add_rms_norm_stats_selfcheck.json``.  The GPU box never reads the reference; the tests read
 only these fixtures.  Case shapes are scaled-down members of the reference's
 own case lists (run_precision_suite.py:19-36, test_lse_flatten_regression.py:31-47,
 lse_merge_cases.py:14-70) so the fixtures stay small.
@@ -117,11 +123,65 @@ def make_merge(ref_dir, out_dir):
     print("lse_merge", len(out) // 6, "cases")
 
 
+def norm_cases():
+    # scaled-down members of add_rms_norm_stats_cases.py:21-30 (same boundary kinds)
+    return [("odd-rows-77", (77, 128)), ("k-min", (7, 16)), ("single-row", (1, 5120)),
+            ("k-not-pow2", (3, 5008)), ("k-2048", (5, 2048))]
+
+
+def make_norm(ref_dir, out_dir):
+    import json
+    import torch
+    tdir = os.path.join(ref_dir, "ascend-kernel/csrc/ops/add_rms_norm_stats/test")
+    sys.path.insert(0, tdir)
+    import add_rms_norm_stats_cases as C  # the reference's own case module
+    import add_rms_norm_stats_ref as R    # the reference's own golden
+    C.DEV = "cpu"                          # the module only uses DEV as a .to() target
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    out = {}
+    for dtype, dname in ((torch.bfloat16, "bf16"), (torch.float16, "fp16")):
+        for name, (m, k) in norm_cases():
+            for mode in (0, 1, 2):
+                for has_beta in ((False, True) if mode == 1 else (False,)):
+                    seed = zlib.crc32(f"norm/{dname}/{name}/{mode}/{has_beta}".encode()) % 2**31
+                    x1, x2, gamma, beta = C.make_inputs(m, k, dtype, seed, has_beta)
+                    x_out, rstd, y = R.cpu_ref(x1, x2, gamma, beta, 1e-6, mode)
+                    key = f"{dname}|{name}|{mode}|{int(has_beta)}"
+                    out[key + "|x1"] = bits(x1)
+                    out[key + "|x2"] = bits(x2)
+                    out[key + "|gamma"] = bits(gamma)
+                    if beta is not None:
+                        out[key + "|beta"] = bits(beta)
+                    out[key + "|rstd"] = rstd.reshape(-1).numpy()
+                    if x_out is not None:
+                        out[key + "|x_out"] = bits(x_out)
+                    if y is not None:
+                        out[key + "|y"] = bits(y)
+    np.savez_compressed(os.path.join(out_dir, "add_rms_norm_stats_cases.npz"), **out)
+    sc = json.load(open(os.path.join(tdir, "f2_golden_selfcheck.json")))
+    keep = {"source": "add_rms_norm_stats/test/f2_golden_selfcheck.json (reference device run: "
+                      + sc["env"] + ", " + sc["date"] + ")",
+            "eps": 1e-6, "mode": 1, "has_beta": False,
+            "seed_rule": "zlib.crc32(f'golden/{torch_dtype}/{case}') % 2**31 "
+                         "(run_golden_selfcheck.py dump_strict_violations)",
+            "element_dumps": [{"dtype": r["dtype"], "case": r["case"], "shape": r["shape"],
+                               "elements": [{f: e[f] for f in ("row", "col", "ref", "cann", "rstd_cann", "gamma")}
+                                            for e in r["elements"]]}
+                              for r in sc["violating_element_dumps"]],
+            "cases": [{"dtype": c["dtype"], "case": c["case"], "shape": c["shape"],
+                       "cann_vs_ref": c["checks"]["cann_vs_ref"], "ours_vs_ref": c["checks"]["ours_vs_ref"]}
+                      for c in sc["cases"]]}
+    with open(os.path.join(out_dir, "add_rms_norm_stats_selfcheck.json"), "w") as f:
+        json.dump(keep, f, indent=1)
+    print("add_rms_norm_stats", len(norm_cases()) * 8, "cases")
+
+
 def main():
     ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     out_dir = os.path.dirname(os.path.abspath(__file__))
     make_stage1(ref_dir, out_dir)
     make_merge(ref_dir, out_dir)
+    make_norm(ref_dir, out_dir)
 
 
 if __name__ == "__main__":

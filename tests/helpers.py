@@ -96,3 +96,25 @@ def kernel_structure(q_len, group, kv_cap_tokens, T, H, KVH, batch, block_cols, 
         split = int(p.split_tokens)
         return 0, dict(segments=lambda kv: O.decode_segments(kv, split=split, tile=64, warps=4))
     return 1, dict(chunk=128, split=int(p.split_tokens))
+
+
+def norm_inputs(m, k, dtype, seed, has_beta):
+    """The seeded inputs of add_rms_norm_stats_cases.make_inputs
+    (add_rms_norm_stats/test/add_rms_norm_stats_cases.py:33-43), drawn on the
+    CPU in the same order: x1, x2 ~ 0.5 N(0,1); gamma ~ 1 + 0.1 N(0,1);
+    beta ~ 0.05 N(0,1). Returns CPU tensors of ``dtype`` (beta None unless
+    has_beta)."""
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x1 = (torch.randn(m, k, generator=g, dtype=torch.float32) * 0.5).to(dtype)
+    x2 = (torch.randn(m, k, generator=g, dtype=torch.float32) * 0.5).to(dtype)
+    gamma = (1.0 + torch.randn(k, generator=g, dtype=torch.float32) * 0.1).to(dtype)
+    beta = (torch.randn(k, generator=g, dtype=torch.float32) * 0.05).to(dtype) if has_beta else None
+    return x1, x2, gamma, beta
+
+
+def bits_to_f64(bits, dtype):
+    """uint16 bit patterns of bf16 / fp16 values -> fp64."""
+    if dtype == "bf16":
+        return O.bf16_bits_to_f64(bits)
+    return np.asarray(bits, dtype=np.uint16).view(np.float16).astype(np.float64)

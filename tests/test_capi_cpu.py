@@ -39,6 +39,8 @@ def test_torch_schemas_match_reference():
                           "(Tensor, Tensor)",
         "f3_gateup_epilogue": "npu::f3_gateup_epilogue(Tensor a, Tensor b, Tensor? workspace, Tensor? out_d, "
                               "int mode) -> (Tensor, Tensor)",
+        "add_rms_norm_stats": "npu::add_rms_norm_stats(Tensor x1, Tensor x2, Tensor? gamma, Tensor? beta, "
+                              "float eps, int mode) -> (Tensor, Tensor, Tensor)",
     }
     for name, schema in want.items():
         op = getattr(torch.ops.npu, name)
@@ -121,3 +123,19 @@ def test_gateup_validation_without_gpu():
     assert "N tile" in capi.last_error()
     assert lib.cascade_f3_gateup_epilogue(None, None, None, None, 128, 16, 48, 128, 1, None) == capi.ERR_INVALID
     assert lib.cascade_f3_gateup_epilogue(None, None, None, None, 128, 16, 64, 128, 2, None) == capi.ERR_WORKSPACE
+
+
+def test_add_rms_norm_stats_validation_without_gpu():
+    """The C ABI rejects, before any launch, what op_host/add_rms_norm_stats.cpp
+    rejects (mode, eps, dtype, empty M, K range, K % 16), with its texts."""
+    from cascade_kernel import capi
+    lib = capi.load()
+    def rc(M=4, K=128, dtype=capi.BF16, mode=0, eps=1e-6):
+        return lib.cascade_add_rms_norm_stats(None, None, None, None, None, None, None, M, K, dtype, mode, eps, None)
+    assert rc(mode=3) == capi.ERR_INVALID and "mode must be 0, 1 or 2" in capi.last_error()
+    assert rc(eps=0.0) == capi.ERR_INVALID and "eps must be > 0" in capi.last_error()
+    assert rc(dtype=capi.FP32) == capi.ERR_INVALID and "bf16 or fp16" in capi.last_error()
+    assert rc(M=0) == capi.ERR_INVALID and "empty row count" in capi.last_error()
+    assert rc(K=5136) == capi.ERR_INVALID and "(0, 5120]" in capi.last_error()
+    assert rc(K=24) == capi.ERR_INVALID and "multiple of 16" in capi.last_error()
+    assert rc() == capi.ERR_INVALID and "null pointer" in capi.last_error()

@@ -23,6 +23,7 @@ EXPORTED = [
     "cascade_decode_step",
     "cascade_lse_merge",
     "cascade_f3_gateup_epilogue",
+    "cascade_add_rms_norm_stats",
     "cascade_last_error",
     "cascade_device_error",
     "cascade_version",
@@ -92,6 +93,8 @@ def load():
     lib.cascade_lse_merge.restype = ctypes.c_int
     lib.cascade_f3_gateup_epilogue.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
     lib.cascade_f3_gateup_epilogue.restype = ctypes.c_int
+    lib.cascade_add_rms_norm_stats.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, ctypes.c_float, vp]
+    lib.cascade_add_rms_norm_stats.restype = ctypes.c_int
     lib.cascade_last_error.argtypes = []
     lib.cascade_last_error.restype = ctypes.c_char_p
     lib.cascade_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
@@ -224,3 +227,10 @@ def lse_merge(o1, o2, lse1, stride1, lse2, stride2, out, rows, dim, stream=None)
 def gateup(a, b, ws, d, d_stride, M, K, I, mode, stream=None):
     return check(load().cascade_f3_gateup_epilogue(
         _ptr(a), _ptr(b), _ptr(ws), _ptr(d), d_stride, M, K, I, mode, stream_ptr(stream)))
+
+
+def add_rms_norm_stats(x1, x2, gamma, beta, x_out, rstd, y, M, K, mode, eps, stream=None):
+    """cascade_add_rms_norm_stats through the C ABI (dtype taken from x1)."""
+    return check(load().cascade_add_rms_norm_stats(
+        _ptr(x1), _ptr(x2), _ptr(gamma), _ptr(beta), _ptr(x_out), _ptr(rstd), _ptr(y), M, K,
+        dtype_code(x1.dtype), mode, eps, stream_ptr(stream)))

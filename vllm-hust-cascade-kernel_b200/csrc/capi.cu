@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -455,6 +456,46 @@ int cascade_lse_merge(const void* o1, int32_t o1_dtype, const void* o2, int32_t 
   L.o2_dtype = o2_dtype;
   L.out_dtype = out_dtype;
   cudaError_t e = launch_lse_merge(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(op, e);
+  return CASCADE_OK;
+}
+
+int cascade_add_rms_norm_stats(const void* x1, const void* x2, const void* gamma, const void* beta, void* x_out,
+                               float* rstd, void* y, int64_t M, int64_t K, int32_t dtype, int32_t mode, float eps,
+                               cascade_stream_t stream) {
+  // op_host/add_rms_norm_stats.cpp:64-104, same limits and texts
+  const char* op = "add_rms_norm_stats";
+  if (mode < 0 || mode > 2) return fail(CASCADE_ERR_INVALID, "%s: mode must be 0, 1 or 2", op);
+  if (!(eps > 0.f)) return fail(CASCADE_ERR_INVALID, "%s: eps must be > 0", op);
+  if (dtype != CASCADE_BF16 && dtype != CASCADE_FP16)
+    return fail(CASCADE_ERR_INVALID, "%s: x1 must be bf16 or fp16", op);
+  if (M <= 0) return fail(CASCADE_ERR_INVALID, "%s: empty row count", op);
+  if (K <= 0 || K > 5120) return fail(CASCADE_ERR_INVALID, "%s: K must be in (0, 5120] (one row resident in UB)", op);
+  if (K % 16 != 0) return fail(CASCADE_ERR_INVALID, "%s: K must be a multiple of 16 (32B row copies)", op);
+  if (M > INT32_MAX) return fail(CASCADE_ERR_UNSUPPORTED, "%s: more than 2^31-1 rows", op);
+  if (!x1 || !rstd) return fail(CASCADE_ERR_INVALID, "%s: null pointer", op);
+  if (mode != 1 && !x2) return fail(CASCADE_ERR_INVALID, "%s: x2 must be contiguous, same shape and dtype as x1", op);
+  if (mode == 0 && !x_out) return fail(CASCADE_ERR_INVALID, "%s: null x_out", op);
+  if (mode == 1 && (!gamma || !y))
+    return fail(CASCADE_ERR_INVALID, "%s: mode 1 needs a contiguous gamma of K elements, same dtype", op);
+  auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+  if (mis(x1) || (mode != 1 && mis(x2)) || (mode == 0 && mis(x_out)) ||
+      (mode == 1 && (mis(gamma) || mis(y) || (beta && mis(beta)))))
+    return fail(CASCADE_ERR_INVALID, "%s: tensors must be 16-byte aligned", op);
+  RmsNormLaunch L;
+  L.x1 = x1;
+  L.x2 = mode == 1 ? nullptr : x2;
+  L.gamma = mode == 1 ? gamma : nullptr;
+  L.beta = mode == 1 ? beta : nullptr;
+  L.x_out = mode == 0 ? x_out : nullptr;
+  L.rstd = rstd;
+  L.y = mode == 1 ? y : nullptr;
+  L.M = static_cast<int32_t>(M);
+  L.K = static_cast<int32_t>(K);
+  L.m_padded = static_cast<int32_t>((M + 7) / 8 * 8);
+  L.mode = mode;
+  L.eps = eps;
+  cudaError_t e = launch_add_rms_norm_stats(L, dtype == CASCADE_FP16, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(op, e);
   return CASCADE_OK;
 }

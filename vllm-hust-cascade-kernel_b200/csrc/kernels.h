@@ -116,6 +116,23 @@ cudaError_t launch_gateup(const GateUpLaunch& p, const void* a, const void* b, c
 cudaError_t launch_gateup_window(const void* ws, void* d, int64_t d_stride, int32_t M, int32_t I, int32_t mode,
                                  cudaStream_t stream);
 
+// ----------------------------------------------------------------------------
+// Residual add + RMSNorm statistics
+// ----------------------------------------------------------------------------
+struct RmsNormLaunch {
+  const void* x1;      // [M, K] 16-bit
+  const void* x2;      // [M, K] (modes 0 and 2)
+  const void* gamma;   // [K] (mode 1)
+  const void* beta;    // [K] or nullptr (mode 1)
+  void* x_out;         // [M, K] (mode 0)
+  float* rstd;         // [m_padded] (rows >= M zeroed)
+  void* y;             // [M, K] (mode 1)
+  int32_t M, K, m_padded, mode;
+  float eps;
+};
+
+cudaError_t launch_add_rms_norm_stats(const RmsNormLaunch& p, bool fp16, cudaStream_t stream);
+
 // Host: raise a kernel's dynamic shared memory limit once per (kernel,
 // device) instead of on every launch.
 cudaError_t ensure_smem_limit(const void* kernel, int bytes);

@@ -308,10 +308,66 @@ at::Tensor cascade_gateup_swiglu(const at::Tensor& x, const at::Tensor& w) {
   return d;
 }
 
+// torch.ops.npu.add_rms_norm_stats: checks, their order and texts and the
+// output allocation of op_host/add_rms_norm_stats.cpp:59-104 -- unused
+// outputs come back as 0-element tensors and rstd is (ceil(M/8)*8, 1) fp32
+// with zeroed padding rows.
+std::tuple<at::Tensor, at::Tensor, at::Tensor> add_rms_norm_stats(const at::Tensor& x1, const at::Tensor& x2,
+                                                                  const c10::optional<at::Tensor>& gamma,
+                                                                  const c10::optional<at::Tensor>& beta, double eps,
+                                                                  int64_t mode) {
+  TORCH_CHECK(x1.dim() == 2, "add_rms_norm_stats: x1 must be 2D (M, K)");
+  TORCH_CHECK(x1.is_contiguous(), "add_rms_norm_stats: x1 must be contiguous");
+  TORCH_CHECK(mode >= 0 && mode <= 2, "add_rms_norm_stats: mode must be 0, 1 or 2");
+  TORCH_CHECK(eps > 0.0, "add_rms_norm_stats: eps must be > 0");
+  const bool is_bf16 = x1.scalar_type() == at::kBFloat16;
+  const bool is_fp16 = x1.scalar_type() == at::kHalf;
+  TORCH_CHECK(is_bf16 || is_fp16, "add_rms_norm_stats: x1 must be bf16 or fp16");
+  if (mode != 1) {
+    TORCH_CHECK(x2.defined() && x2.is_contiguous() && x2.sizes() == x1.sizes() &&
+                    x2.scalar_type() == x1.scalar_type(),
+                "add_rms_norm_stats: x2 must be contiguous, same shape and dtype as x1");
+  }
+  const int64_t M = x1.size(0), K = x1.size(1);
+  TORCH_CHECK(M > 0, "add_rms_norm_stats: empty row count");
+  TORCH_CHECK(K > 0 && K <= 5120, "add_rms_norm_stats: K must be in (0, ", 5120, "] (one row resident in UB)");
+  TORCH_CHECK(K % 16 == 0, "add_rms_norm_stats: K must be a multiple of 16 (32B row copies)");
+  const bool has_beta = mode == 1 && beta.has_value() && beta->defined() && beta->numel() > 0;
+  if (mode == 1) {
+    TORCH_CHECK(gamma.has_value() && gamma->defined() && gamma->is_contiguous() && gamma->numel() == K &&
+                    gamma->scalar_type() == x1.scalar_type(),
+                "add_rms_norm_stats: mode 1 needs a contiguous gamma of K elements, same dtype");
+    if (has_beta) {
+      TORCH_CHECK(beta->is_contiguous() && beta->numel() == K && beta->scalar_type() == x1.scalar_type(),
+                  "add_rms_norm_stats: beta must be contiguous, K elements, same dtype");
+    }
+  }
+  TORCH_CHECK(x1.is_cuda(), "add_rms_norm_stats: x1 must be a CUDA tensor");
+  const int dev = x1.get_device();
+  TORCH_CHECK(mode == 1 || (x2.is_cuda() && x2.get_device() == dev), "add_rms_norm_stats: x2 must be on x1's device");
+  TORCH_CHECK(mode != 1 || (gamma->is_cuda() && gamma->get_device() == dev &&
+                            (!has_beta || (beta->is_cuda() && beta->get_device() == dev))),
+              "add_rms_norm_stats: gamma/beta must be on x1's device");
+  const c10::cuda::CUDAGuard guard(x1.device());
+  const int64_t m_padded = (M + 7) / 8 * 8;
+  auto x_out = mode == 0 ? at::empty_like(x1) : at::empty({0}, x1.options());
+  auto rstd = at::empty({m_padded, 1}, x1.options().dtype(at::kFloat));
+  auto y = mode == 1 ? at::empty_like(x1) : at::empty({0}, x1.options());
+  check_rc(cascade_add_rms_norm_stats(x1.data_ptr(), mode == 1 ? nullptr : x2.data_ptr(),
+                                      mode == 1 ? gamma->data_ptr() : nullptr, has_beta ? beta->data_ptr() : nullptr,
+                                      mode == 0 ? x_out.data_ptr() : nullptr, rstd.data_ptr<float>(),
+                                      mode == 1 ? y.data_ptr() : nullptr, M, K, dtype_code(x1.scalar_type()),
+                                      static_cast<int32_t>(mode), static_cast<float>(eps), current_stream(x1)));
+  return {x_out, rstd, y};
+}
+
 }  // namespace
 }  // namespace cascade_torch
 
 TORCH_LIBRARY_FRAGMENT(npu, m) {
+  m.def(
+      "add_rms_norm_stats(Tensor x1, Tensor x2, Tensor? gamma, Tensor? beta, float eps, "
+      "int mode) -> (Tensor, Tensor, Tensor)");
   m.def("lse_merge(Tensor o1, Tensor o2, Tensor lse1, Tensor lse2, int out_code=0) -> Tensor");
   m.def(
       "fa_fp32_stage1(Tensor query, Tensor key, Tensor value, Tensor block_table, "
@@ -342,4 +398,5 @@ TORCH_LIBRARY_IMPL(npu, CUDA, m) {
   m.impl("cascade_lse_merge", TORCH_FN(cascade_torch::cascade_lse_merge));
   m.impl("cascade_gateup_swiglu", TORCH_FN(cascade_torch::cascade_gateup_swiglu));
   m.impl("cascade_decode_step", TORCH_FN(cascade_torch::cascade_decode_step));
+  m.impl("add_rms_norm_stats", TORCH_FN(cascade_torch::add_rms_norm_stats));
 }
