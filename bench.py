@@ -308,6 +308,8 @@ def run_ours(args, rank, world, local):
     mlp70 = (gateup_sweep(flush, peaks, Ms=(256,), K=8192, I=28672 // world, seed=11 + rank)
              if not args.no_gateup and 28672 % (128 * world) == 0 else None)
 
+    norm = norm_sweep(flush, peaks) if not args.no_gateup else None
+
     verify = verify_sharded(args, rank, world, outs[0]) if world > 1 else None
     del graph
 
@@ -377,6 +379,9 @@ def run_ours(args, rank, world, local):
                           f"silu(gate)*up bf16 [256,{28672 // world}] per rank ({world} rank(s))")
         line["gateup_swiglu_70b_shard"] = mlp70
         line["gpu_launches"] += mlp70.pop("_launches")
+    if norm is not None:
+        line["add_rms_norm_stats"] = norm
+        line["gpu_launches"] += norm.pop("_launches")
     if cpu is not None:
         line["cpu_baseline"] = cpu
     if verify is not None:
@@ -424,6 +429,43 @@ def verify_sharded(args, rank, world, out_local):
         res["gateup_equal_to_single_gpu"] = mlp_ok
     dist.barrier()
     return res
+
+
+def norm_sweep(flush, peaks, reps=5, seed=5):
+    """add_rms_norm_stats (npu.add_rms_norm_stats, one kernel per call) on the
+    reference's two production shapes (add_rms_norm_stats_cases.py:21-22:
+    prefill 2048 x 5120, decode 32 x 5120, bf16), every mode; L2 flushed
+    before each timed call. Bytes = inputs read + outputs written."""
+    import torch
+    npu = torch.ops.npu
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    res, launches = {}, 0
+    for name, (M, K) in (("prefill", (2048, 5120)), ("decode", (32, 5120))):
+        x1 = (torch.randn(M, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+        x2 = (torch.randn(M, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+        gamma = (1.0 + torch.randn(K, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+        beta = (torch.randn(K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+        for mode in (0, 1, 2):
+            fn = lambda: npu.add_rms_norm_stats(x1, x2, gamma, beta, 1e-6, mode)
+            for _ in range(3):
+                fn()
+            ts = []
+            for _ in range(reps):
+                flush()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b) * 1e3)
+                launches += 1
+            ts.sort()
+            us = ts[len(ts) // 2]
+            byts = {0: 3 * M * K * 2, 1: 2 * M * K * 2 + 2 * K * 2, 2: 2 * M * K * 2}[mode] + 4 * ((M + 7) // 8 * 8)
+            res[f"{name}_mode{mode}"] = {"us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
+                                         "frac_hbm": round(byts / us / 1e3 / peaks["hbm_gbs"], 4)}
+    return {"shape": "bf16 rows x 5120: prefill M=2048, decode M=32; mode 0 residual+stats, 1 stats+apply "
+                     "(gamma, beta), 2 stats only", "per_case": res, "_launches": launches}
 
 
 def gateup_sweep(flush, peaks, Ms=(1, 16, 64, 256, 4096), K=4096, I=14336, reps=5, seed=7):
@@ -543,7 +585,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-gateup", action="store_true", help="skip the gate_up SwiGLU sweep")
+    ap.add_argument("--no-gateup", action="store_true",
+                    help="skip the gate_up SwiGLU and add_rms_norm_stats sweeps")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))
