@@ -198,7 +198,11 @@ CASCADE_API int cascade_version(void);
  * that size grids): which kernel serves a paged-attention call and how it is
  * split. No CUDA calls. Returns 0 or CASCADE_ERR_*; the fields are:
  *   kernel: 0 = decode path (<= 16 query rows per request and kv head),
- *           1 = tcgen05 tile path (more rows);
+ *           1 = tcgen05 tile path (more rows),
+ *           2 = planned decode path (decode rows, uniform q length, at least
+ *               2048 (request, kv head) pairs and more than one 512-token
+ *               split: a device-built list of the non-empty (request, split)
+ *               items, two persistent CTAs per SM);
  *   rows_per_group: max query rows per (request, kv head) = q_len * H/KVH;
  *   split_tokens: kv tokens per split (a multiple of the kernel's KV tile);
  *   num_splits: splits per request; workspace_bytes: as the *_workspace_size

@@ -92,7 +92,7 @@ def kernel_structure(q_len, group, kv_cap_tokens, T, H, KVH, batch, block_cols, 
                                    block_cols=block_cols))
     desc.q_seqlen_value = 0
     p = C.plan(desc, q_len, suffix)
-    if p.kernel == 0:
+    if p.kernel in (0, 2):  # decode, one CTA per item or planned
         split = int(p.split_tokens)
         return 0, dict(segments=lambda kv: O.decode_segments(kv, split=split, tile=64, warps=4))
     return 1, dict(chunk=128, split=int(p.split_tokens))

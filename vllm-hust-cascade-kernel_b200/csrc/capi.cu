@@ -65,10 +65,25 @@ constexpr int kMaxSplits = 32;     // per request; the step combine merges up to
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Planned decode (kernel 2): uniform-q requests whose one-CTA-per-item grid
+// at 512-token splits would exceed 16384 CTAs (~55 waves of two per SM). That
+// grid is sized by the LONGEST request, so on such wide ragged batches most
+// of its split CTAs find no work (C5: 36,864 CTAs, 4,968 with work); the
+// planned form lists the non-empty items on the device and runs two
+// persistent CTAs per SM over them. Narrower grids keep the per-item kernel
+// (C4-like, 8,192 slots: 186 us widened per-item vs 202 us planned).
+bool decode_planned(const cascade_paged_attn_t* p) {
+  const int64_t cap = p->block_cols * p->block_size;
+  return p->q_seqlen_value > 0 && cap > kDecodeSplit &&
+         p->batch * p->kv_heads * ceil_div(cap, kDecodeSplit) > 16384;
+}
+
 // Shape-only split rule of each kernel.
 void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens, int64_t* num_splits) {
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
-  if (kernel == 0) {
+  if (kernel == 2) {
+    *split_tokens = std::max<int64_t>(kDecodeSplit, ceil_div(ceil_div(cap, kMaxSplits), 64) * 64);
+  } else if (kernel == 0) {
     // 512-token splits, widened (in 64-token tiles) so no request has more than
     // kMaxSplits. When the (request, kv head) pairs alone fill the GPU many
     // times over, splits of 1024 (>= 2048 pairs) or 2048 tokens (>= 4096
@@ -88,10 +103,15 @@ void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens
   *num_splits = ceil_div(cap, *split_tokens);
 }
 
-size_t workspace_for(const cascade_paged_attn_t* p, int64_t num_splits) {
+// Partials [nsplit][rows][128] fp32 + LSE [nsplit][rows]; a planned decode
+// adds its item list [batch * nsplit], the item count and one counter per kv
+// head (int32).
+size_t workspace_for(const cascade_paged_attn_t* p, int64_t num_splits, int kernel) {
   if (num_splits <= 1 && !(p->flags & CASCADE_FLAG_PARTIALS_ONLY)) return 0;
   const size_t rows = static_cast<size_t>(p->num_tokens) * p->num_heads;
-  return static_cast<size_t>(num_splits) * rows * (kHeadDim + 1) * sizeof(float);
+  size_t bytes = static_cast<size_t>(num_splits) * rows * (kHeadDim + 1) * sizeof(float);
+  if (kernel == 2) bytes += (static_cast<size_t>(p->batch) * num_splits + 1 + p->kv_heads) * sizeof(int32_t);
+  return bytes;
 }
 
 // Validation common to both paged-attention entry points; `op` prefixes messages.
@@ -221,10 +241,16 @@ int check_workspace(const char* op, void* ws, size_t ws_bytes, size_t need) {
   return CASCADE_OK;
 }
 
-void set_partials(PagedAttnLaunch* L, void* ws) {
+void set_partials(PagedAttnLaunch* L, void* ws, int kernel) {
   const size_t nrows = static_cast<size_t>(L->num_tokens) * L->num_heads;
   L->part_o = static_cast<float*>(ws);
   L->part_lse = ws ? static_cast<float*>(ws) + static_cast<size_t>(L->num_splits) * nrows * kHeadDim : nullptr;
+  L->plan_items = L->plan_count = L->plan_counters = nullptr;
+  if (kernel == 2 && ws) {
+    L->plan_items = reinterpret_cast<int32_t*>(L->part_lse + static_cast<size_t>(L->num_splits) * nrows);
+    L->plan_count = L->plan_items + static_cast<size_t>(L->batch) * L->num_splits;
+    L->plan_counters = L->plan_count + 1;
+  }
 }
 
 cudaError_t launch_attention(const PagedAttnLaunch& L, int kernel, bool fp16, cudaStream_t stream) {
@@ -243,7 +269,7 @@ int run_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, void* 
   if (rc) return rc;
   L.out = out;
   L.lse = lse;
-  set_partials(&L, ws);
+  set_partials(&L, ws, plan.kernel);
   cudaError_t e = launch_attention(L, plan.kernel, p->dtype == CASCADE_FP16, stream);
   if (e == cudaSuccess && plan.num_splits > 1 && !partials_only) e = launch_split_combine(L, stream);
   if (e != cudaSuccess) return cuda_fail(op, e);
@@ -314,10 +340,10 @@ int cascade_plan_paged_attn(const cascade_paged_attn_t* p, int64_t max_q_seqlen,
   if (!plan) return fail(CASCADE_ERR_INVALID, "%s: null plan", op);
   const int64_t group = p->num_heads / p->kv_heads;
   const int64_t rows = std::max<int64_t>(1, max_q_seqlen) * group;
-  plan->kernel = rows <= 16 ? 0 : 1;
+  plan->kernel = rows <= 16 ? (decode_planned(p) ? 2 : 0) : 1;
   plan->rows_per_group = static_cast<int32_t>(std::min<int64_t>(rows, INT32_MAX));
   split_rule(p, plan->kernel, &plan->split_tokens, &plan->num_splits);
-  plan->workspace_bytes = workspace_for(p, plan->num_splits);
+  plan->workspace_bytes = workspace_for(p, plan->num_splits, plan->kernel);
   return CASCADE_OK;
 }
 
@@ -335,7 +361,7 @@ static size_t workspace_size_any(const cascade_paged_attn_t* p, int suffix) {
   for (int k = 0; k < 2; ++k) {
     int64_t st, ns;
     split_rule(p, k, &st, &ns);
-    best = std::max(best, workspace_for(p, ns));
+    best = std::max(best, workspace_for(p, ns, k));
   }
   return best;
 }
@@ -392,8 +418,8 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
   const size_t need_b = pb.num_splits ? align_up(pb.workspace_bytes, 256) : 0;
   rc = check_workspace(op, workspace, workspace_bytes, need_a + need_b);
   if (rc) return rc;
-  set_partials(&La, workspace);
-  set_partials(&Lb, static_cast<uint8_t*>(workspace) + need_a);
+  set_partials(&La, workspace, pa.kernel);
+  set_partials(&Lb, static_cast<uint8_t*>(workspace) + need_a, pb.kernel);
   const bool fp16 = suffix->dtype == CASCADE_FP16;
   if ((pa.num_splits ? La.num_splits : 0) + (pb.num_splits ? Lb.num_splits : 0) > 64)
     return fail(CASCADE_ERR_UNSUPPORTED, "%s: more than 64 KV splits per row", op);

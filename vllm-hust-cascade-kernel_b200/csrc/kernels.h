@@ -34,6 +34,10 @@ struct PagedAttnLaunch {
   int32_t partial_out;  // 1: always write split partials (a later combine produces the output)
   int32_t pdl;          // 1: launched as a programmatic dependent of the previous kernel in the stream
   float scale_log2;     // softmax scale * log2(e)
+  // planned decode (kernel 2): workspace arrays after the partials, or null
+  int32_t* plan_items;     // [batch * num_splits] (request << 8) | split of the non-empty items
+  int32_t* plan_count;     // number of items
+  int32_t* plan_counters;  // [kv_heads] next item per kv head
 };
 
 cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream);

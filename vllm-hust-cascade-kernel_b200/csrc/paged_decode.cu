@@ -18,6 +18,8 @@
 // Each warp runs its own online softmax over its tokens in 16-token steps;
 // the CPU oracle reproduces this structure exactly (chunk 16, segments =
 // the warp's token subsets).
+#include <algorithm>
+
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -64,15 +66,23 @@ __device__ __forceinline__ void store_out(void* out, int out_dtype, size_t idx, 
   }
 }
 
-template <bool kFp16>
-__device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  DecodeBarriers* bars = reinterpret_cast<DecodeBarriers*>(smem + kStages * kStageBytes);
+__device__ __forceinline__ void init_decode_barriers(DecodeBarriers* bars) {
+  for (int s = 0; s < kStages; ++s) {
+    mbar_init(&bars->full[s], 1);
+    mbar_init(&bars->empty[s], kConsumerWarps);
+  }
+  fence_mbar_init();
+}
 
-  const int split = blockIdx.x;
-  const int g = blockIdx.y;
-  const int b = blockIdx.z;
+// One (split, kv head, request) item. `it0` = tiles this CTA consumed in
+// earlier items (the ring's barrier phases continue across items);
+// `init_bars` initialises the ring barriers first (one item per CTA). Returns
+// the tiles consumed. All 160 threads call it; on return every tile of the
+// item has landed and the ring's shared memory is free again only after a
+// CTA barrier (the merge reuses it).
+template <bool kFp16>
+__device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8_t* smem, DecodeBarriers* bars,
+                                                 int split, int g, int b, uint32_t it0, bool init_bars) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -118,17 +128,13 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
         p.lse[(static_cast<size_t>(t) * p.num_heads + h) * p.lse_stride + c] = -INFINITY;
       }
     }
-    return;
+    return 0;
   }
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], kConsumerWarps);
-    }
-    fence_mbar_init();
+  if (init_bars) {
+    if (threadIdx.x == 0) init_decode_barriers(bars);
+    __syncthreads();
   }
-  __syncthreads();
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -153,8 +159,9 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
       const int oob_row = p.num_blocks * bs;  // fully out of range -> zero fill
       const uint64_t pol = policy_evict_first();
       for (int i = 0; i < ntiles; ++i) {
-        const int st = i % kStages;
-        if (i >= kStages) mbar_wait(&bars->empty[st], ((i / kStages) - 1) & 1);
+        const uint32_t gi = it0 + i;  // ring position of this tile in the CTA's lifetime
+        const int st = gi % kStages;
+        if (gi >= kStages) mbar_wait(&bars->empty[st], ((gi / kStages) - 1) & 1);
         uint8_t* sk = smem + st * kStageBytes;
         uint8_t* sv = sk + kKBytes;
         mbar_arrive_expect_tx(&bars->full[st], kStageBytes);
@@ -174,7 +181,7 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
         }
       }
     }
-    return;
+    return ntiles;
   }
 
   // -------------------------------------------------------------- consumers
@@ -226,8 +233,9 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
   const int mi = lane >> 3, mr = lane & 7;
 
   for (int i = 0; i < ntiles; ++i) {
-    const int st = i % kStages;
-    mbar_wait(&bars->full[st], (i / kStages) & 1);
+    const uint32_t gi = it0 + i;
+    const int st = gi % kStages;
+    mbar_wait(&bars->full[st], (gi / kStages) & 1);
     const uint32_t kbase = smem_base + st * kStageBytes;
     const uint32_t vbase = kbase + kKBytes;
 
@@ -388,13 +396,110 @@ __device__ __forceinline__ void paged_decode_body(const PagedAttnLaunch& p) {
       for (int cc = c; cc < p.lse_stride; cc += kHeadDim / 4) p.lse[row * p.lse_stride + cc] = lse_nat;
     }
   }
+  return ntiles;
 }
 
+__device__ __forceinline__ uint8_t* decode_smem() {
+  extern __shared__ uint8_t smem_raw[];
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+}
+
+// One CTA per (split, kv head, request).
 template <bool kFp16>
 __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_constant__ PagedAttnLaunch p) {
   pdl_launch_dependents();
-  paged_decode_body<kFp16>(p);
+  uint8_t* smem = decode_smem();
+  DecodeBarriers* bars = reinterpret_cast<DecodeBarriers*>(smem + kStages * kStageBytes);
+  paged_decode_item<kFp16>(p, smem, bars, blockIdx.x, blockIdx.y, blockIdx.z, 0u, true);
   if (p.pdl && threadIdx.x == 0) pdl_wait();
+}
+
+// Planned form for wide ragged batches: decode_plan_kernel (launched just
+// before, this kernel being its programmatic dependent) lists the non-empty
+// (request, split) items; gridDim.x CTAs per kv head (two per SM in all) take
+// items from a per-kv-head counter, and first write -inf partial LSEs for the
+// empty split slots of the requests b = blockIdx.x (mod gridDim.x), so the
+// combine sees every slot. No CTA is launched for an empty split.
+template <bool kFp16>
+__global__ void __launch_bounds__(kThreads, 2) paged_decode_planned_kernel(const __grid_constant__ PagedAttnLaunch p) {
+  pdl_launch_dependents();
+  uint8_t* smem = decode_smem();
+  DecodeBarriers* bars = reinterpret_cast<DecodeBarriers*>(smem + kStages * kStageBytes);
+  __shared__ int32_t sh_item;
+  const int g = blockIdx.y;
+  if (threadIdx.x == 0) init_decode_barriers(bars);
+  pdl_wait();  // the item list, its count and the zeroed counters are complete
+  __syncthreads();
+  const size_t plane = static_cast<size_t>(p.num_tokens) * p.num_heads;
+  for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
+    const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
+    const int used = kv > 0 ? min(p.num_splits, (kv + p.split_tokens - 1) / p.split_tokens) : 0;
+    const int nrows = p.q_seqlen_value * p.group;
+    const int tok0 = b * p.q_seqlen_value;
+    for (int i = threadIdx.x; i < (p.num_splits - used) * nrows; i += blockDim.x) {
+      const int s = used + i / nrows, r = i % nrows;
+      const int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+      p.part_lse[static_cast<size_t>(s) * plane + static_cast<size_t>(t) * p.num_heads + h] = -INFINITY;
+    }
+  }
+  const int count = *p.plan_count;
+  uint32_t it0 = 0;
+  for (;;) {
+    if (threadIdx.x == 0) sh_item = atomicAdd(p.plan_counters + g, 1);
+    __syncthreads();
+    const int item = sh_item;
+    if (item >= count) break;
+    const int32_t code = p.plan_items[item];
+    it0 += paged_decode_item<kFp16>(p, smem, bars, code & 0xFF, g, code >> 8, it0, false);
+    __syncthreads();  // the merge used the ring; the next item's loads may start
+  }
+}
+
+// Lists the non-empty (request, split) items of a planned decode: request b
+// contributes min(num_splits, ceil(kv_b / split_tokens)) items (none for
+// kv_b = 0), coded (b << 8) | split, in request order; also the count, and
+// zeroes the per-kv-head item counters. One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) decode_plan_kernel(const __grid_constant__ PagedAttnLaunch p) {
+  pdl_launch_dependents();
+  if (p.pdl) pdl_wait();  // the seqlens may come from the kernel before
+  __shared__ int32_t wsum[32];
+  __shared__ int32_t carry;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) carry = 0;
+  for (int i = tid; i < p.kv_heads; i += blockDim.x) p.plan_counters[i] = 0;
+  __syncthreads();
+  for (int base = 0; base < p.batch; base += blockDim.x) {
+    const int b = base + tid;
+    int n = 0;
+    if (b < p.batch) {
+      const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
+      n = kv > 0 ? min(p.num_splits, (kv + p.split_tokens - 1) / p.split_tokens) : 0;
+    }
+    int x = n;  // inclusive scan: warp, then warp totals
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int v = lane < (blockDim.x >> 5) ? wsum[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      wsum[lane] = v;  // inclusive prefix of warp totals
+    }
+    __syncthreads();
+    const int excl = carry + (w > 0 ? wsum[w - 1] : 0) + x - n;
+    for (int s = 0; s < n; ++s) p.plan_items[excl + s] = (b << 8) | s;
+    __syncthreads();
+    if (tid == 0) carry += wsum[(blockDim.x >> 5) - 1];
+    __syncthreads();
+  }
+  if (tid == 0) *p.plan_count = carry;
 }
 
 // One warp per (token, head) row: merge the split partials.
@@ -444,6 +549,18 @@ __global__ void split_combine_kernel(const __grid_constant__ PagedAttnLaunch p) 
 }  // namespace
 
 cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream) {
+  if (p.plan_items != nullptr) {
+    // plan (one CTA), then the persistent decode as its programmatic
+    // dependent: two CTAs per SM in all, split evenly over the kv heads
+    launch_maybe_pdl(decode_plan_kernel, dim3(1), dim3(1024), 0, stream, p.pdl != 0, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    auto kern = fp16 ? paged_decode_planned_kernel<true> : paged_decode_planned_kernel<false>;
+    e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
+    if (e != cudaSuccess) return e;
+    const int per_head = std::max(1, (2 * kNumSMs) / std::max(1, p.kv_heads));
+    return launch_maybe_pdl(kern, dim3(per_head, p.kv_heads, 1), dim3(kThreads), kSmemBytes, stream, true, p);
+  }
   dim3 grid(p.num_splits, p.kv_heads, p.batch);
   auto kern = fp16 ? paged_decode_kernel<true> : paged_decode_kernel<false>;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
