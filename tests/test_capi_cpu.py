@@ -139,3 +139,23 @@ def test_add_rms_norm_stats_validation_without_gpu():
     assert rc(K=5136) == capi.ERR_INVALID and "(0, 5120]" in capi.last_error()
     assert rc(K=24) == capi.ERR_INVALID and "multiple of 16" in capi.last_error()
     assert rc() == capi.ERR_INVALID and "null pointer" in capi.last_error()
+
+
+def test_planner_planned_decode_choice_and_workspace():
+    """Kernel 2 (planned decode) exactly when the uniform-q one-CTA-per-item
+    grid at 512-token splits would exceed 16384 CTAs; its workspace adds the
+    item list [batch * splits], the count and one counter per kv head."""
+    from cascade_kernel import capi
+    def plan(B, cols, bs=16, KVH=8, q=1):
+        d = _desc(num_tokens=B * q, batch=B, kv_heads=KVH, num_heads=KVH * 5, block_size=bs, block_cols=cols,
+                  q_seqlen_value=q)
+        return capi.plan(d, q, True)
+    p = plan(512, 290)                       # C5-like: 4096 pairs x 10 splits
+    assert (p.kernel, p.split_tokens, p.num_splits) == (2, 512, 10)
+    rows = 512 * 40
+    assert p.workspace_bytes == 10 * rows * 129 * 4 + (512 * 10 + 1 + 8) * 4
+    assert plan(256, 16, bs=128).kernel == 0   # C4-like: 2048 pairs x 4 splits = 8192
+    assert plan(512, 32, bs=16).kernel == 0    # one split only
+    assert plan(64, 8, bs=128, KVH=8).kernel == 0
+    d = _desc(num_tokens=512, batch=512, kv_heads=8, num_heads=40, block_size=16, block_cols=290, q_seqlen_value=0)
+    assert capi.plan(d, 1, True).kernel == 0  # per-request q lengths: never planned
