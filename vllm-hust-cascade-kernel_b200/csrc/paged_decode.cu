@@ -5,7 +5,10 @@
 // Memory-bound design (KV bytes dominate):
 //  * one CTA per (split of 512 kv tokens, kv head, request); the split's
 //    partial (O, LSE) is merged by launch_split_combine when a request has
-//    more than one split;
+//    more than one split. For wide ragged batches a planned form instead
+//    lists the non-empty (request, split) items on the device
+//    (decode_plan_kernel) and runs two persistent CTAs per SM over them
+//    (paged_decode_planned_kernel), with the same per-item code;
 //  * a producer warp streams 64-token K/V tiles with 2-D TMA (one box per page
 //    segment and 64-element half of the head dim, 128-byte swizzle) into a
 //    3-stage ring: 32 KB per stage, 96 KB per CTA, two CTAs per SM;
