@@ -135,3 +135,30 @@ def test_swiglu_llama8b_shapes_vs_torch_fp32(M):
     C.gateup(x, w, None, d2, I, M, K, I, 1)
     torch.cuda.synchronize()
     assert torch.equal(d, d2)
+
+
+@pytest.mark.parametrize("M,K,I", [(200, 4096, 14336), (256, 8192, 3584), (129, 1024, 640), (256, 64, 128)])
+def test_swiglu_256_row_forms(M, K, I):
+    """129..256 rows (the 256-row tile with a shared W tile, or the 128-row
+    forms the launcher picks by tile count), K from one block to 8192:
+    within one bf16 ulp of torch fp32 (+ GEMM order noise), bit-identical on
+    a second call, no device error, and the C ABI equal to the op."""
+    import torch
+    Hh.need_cuda()
+    npu = Hh.ops()
+    C = Hh.capi()
+    x, w = _inputs(M, K, I, seed=M + K + I)
+    d = npu.cascade_gateup_swiglu(x, w)
+    d_again = npu.cascade_gateup_swiglu(x, w)
+    c = x.float() @ w.float().t()
+    g, u = c[:, :I], c[:, I:]
+    ref = (g / (1 + torch.exp(-g)) * u)
+    err = (d.float() - ref).abs()
+    bound = torch.maximum(ref.abs(), d.float().abs()) * 2.0 ** -7 + 1e-4
+    assert bool((err <= bound).all()), float((err - bound).max())
+    assert torch.equal(d, d_again)
+    d2 = torch.empty_like(d)
+    C.gateup(x, w, None, d2, I, M, K, I, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(d, d2)
+    assert C.device_error() == 0
