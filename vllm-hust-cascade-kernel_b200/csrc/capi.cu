@@ -96,7 +96,11 @@ void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens
     const int64_t group = p->num_heads / p->kv_heads;
     const int64_t mtiles = std::max<int64_t>(p->batch, ceil_div(p->num_tokens * group, 128));
     const int64_t units = p->kv_heads * mtiles;
-    const int64_t want = ceil_div(kNumSMs, units);  // one 225 KB CTA per SM
+    // Enough splits for one 225 KB CTA per SM, and at least two: the grid is
+    // sized by the longest request, and on ragged prefixes (C5) the longest
+    // requests' CTAs set the kernel's length (C5 step 297 -> 276 us with two
+    // splits; uniform shapes with >= 148 row tiles lose ~4% to the extra wave).
+    const int64_t want = std::max<int64_t>(2, ceil_div(kNumSMs, units));
     int64_t ns = std::min<int64_t>(std::min<int64_t>(std::max<int64_t>(want, 1), ceil_div(cap, kTcTile)), kMaxSplits);
     *split_tokens = ceil_div(ceil_div(cap, ns), kTcTile) * kTcTile;
   }
