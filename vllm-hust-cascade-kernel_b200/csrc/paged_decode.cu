@@ -8,7 +8,9 @@
 //    more than one split. For wide ragged batches a planned form instead
 //    lists the non-empty (request, split) items on the device
 //    (decode_plan_kernel) and runs two persistent CTAs per SM over them
-//    (paged_decode_planned_kernel), with the same per-item code;
+//    (paged_decode_stream_kernel: a fetcher warp prepares the next item in
+//    shared memory while the current one streams through a ring that never
+//    drains between items), with the same tile and merge code;
 //  * a producer warp streams 64-token K/V tiles with 2-D TMA (one box per page
 //    segment and 64-element half of the head dim, 128-byte swizzle) into a
 //    3-stage ring: 32 KB per stage, 96 KB per CTA, two CTAs per SM;
@@ -77,122 +79,69 @@ __device__ __forceinline__ void init_decode_barriers(DecodeBarriers* bars) {
   fence_mbar_init();
 }
 
-// One (split, kv head, request) item. `it0` = tiles this CTA consumed in
-// earlier items (the ring's barrier phases continue across items);
-// `init_bars` initialises the ring barriers first (one item per CTA). Returns
-// the tiles consumed. All 160 threads call it; on return every tile of the
-// item has landed and the ring's shared memory is free again only after a
-// CTA barrier (the merge reuses it).
-template <bool kFp16>
-__device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8_t* smem, DecodeBarriers* bars,
-                                                 int split, int g, int b, uint32_t it0, bool init_bars) {
-  const int warp = threadIdx.x >> 5;
+// Producer warp of one item: pulls the split's block-table entries
+// (bt_pre0/1 = entries lane and lane + 32, loaded earlier by this warp) into
+// shared memory, then lane 0 streams the item's tiles into the NS-stage ring
+// at ring positions it0, it0 + 1, ...
+template <int NS, bool kBtFilled = false>
+__device__ __forceinline__ void produce_tiles(const PagedAttnLaunch& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                              int32_t* bt_smem, int b, int g, int s_begin, int s_end, int kv,
+                                              int ntiles, uint32_t it0, int bt_pre0, int bt_pre1) {
   const int lane = threadIdx.x & 31;
-
-  // The split's block-table entries do not depend on the kv length: the
-  // producer warp issues their load first, so it overlaps the length load.
-  const int s_begin = split * p.split_tokens;
   const int first_page = s_begin / p.block_size;
-  const int bt_avail = min(kBtCache, p.block_cols - first_page);
-  int bt_pre0 = 0, bt_pre1 = 0;
-  if (warp == kConsumerWarps) {
-    const int32_t* btrow = p.block_table + static_cast<size_t>(b) * p.block_cols + first_page;
-    if (lane < bt_avail) bt_pre0 = btrow[lane];
-    if (lane + 32 < bt_avail) bt_pre1 = btrow[lane + 32];
+  // The whole warp first pulls this split's block-table entries into shared
+  // memory, so the TMA issue loop never waits on a dependent global load.
+  const int bs = p.block_size;
+  const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
+  const int npages = (kv + bs - 1) / bs;
+  const int last_page = min(npages, (s_end + bs - 1) / bs);  // exclusive
+  const int nbt = last_page - first_page;
+  const bool cached = nbt <= kBtCache;
+  if (cached && !kBtFilled) {
+    static_assert(kBtCache <= 64, "two prefetched entries per lane");
+    if (lane < nbt) bt_smem[lane] = bt_pre0;
+    if (lane + 32 < nbt) bt_smem[lane + 32] = bt_pre1;
   }
-
-  // kv is clamped to the block table's capacity, so no entry past a row is read
-  const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
-  const int q_len = p.q_seqlen_value > 0 ? p.q_seqlen_value : static_cast<int>(p.q_seqlens[b]);
-  const int nrows = q_len * p.group;
-  const int tok0 = request_token_offset(p, b);
-  const int s_end = min(kv, s_begin + p.split_tokens);
-  const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
-
-  // Empty split (kv shorter than this split's start, or no query rows):
-  // write -inf partials so the combine step skips it.
-  if (ntiles == 0 || nrows == 0) {
-    if (p.num_splits > 1 || p.partial_out) {
-      for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
-        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
-        p.part_lse[static_cast<size_t>(split) * p.num_tokens * p.num_heads + static_cast<size_t>(t) * p.num_heads + h] =
-            -INFINITY;
-      }
-    } else {
-      // single split: kv == 0 -> out = 0, lse = -inf
-      for (int i = threadIdx.x; i < nrows * kHeadDim / 2; i += blockDim.x) {
-        int r = i / (kHeadDim / 2), d = (i % (kHeadDim / 2)) * 2;
-        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
-        store_out<kFp16>(p.out, p.out_dtype, (static_cast<size_t>(t) * p.num_heads + h) * kHeadDim + d, 0.f, 0.f);
-      }
-      for (int i = threadIdx.x; i < nrows * p.lse_stride; i += blockDim.x) {
-        int r = i / p.lse_stride, c = i % p.lse_stride;
-        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
-        p.lse[(static_cast<size_t>(t) * p.num_heads + h) * p.lse_stride + c] = -INFINITY;
-      }
-    }
-    return 0;
-  }
-
-  if (init_bars) {
-    if (threadIdx.x == 0) init_decode_barriers(bars);
-    __syncthreads();
-  }
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    // The whole warp first pulls this split's block-table entries into shared
-    // memory, so the TMA issue loop never waits on a dependent global load.
-    const int bs = p.block_size;
-    const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
-    const int npages = (kv + bs - 1) / bs;
-    const int last_page = min(npages, (s_end + bs - 1) / bs);  // exclusive
-    const int nbt = last_page - first_page;
-    const bool cached = nbt <= kBtCache;
-    if (cached) {
-      static_assert(kBtCache <= 64, "two prefetched entries per lane");
-      if (lane < nbt) bars->bt[lane] = bt_pre0;
-      if (lane + 32 < nbt) bars->bt[lane + 32] = bt_pre1;
-    }
-    __syncwarp();
-    if (lane == 0) {
-      tma_prefetch_desc(&p.tmap_k);
-      tma_prefetch_desc(&p.tmap_v);
-      const int box_rows = bs < kTile ? bs : kTile;
-      const int oob_row = p.num_blocks * bs;  // fully out of range -> zero fill
-      const uint64_t pol = policy_evict_first();
-      for (int i = 0; i < ntiles; ++i) {
-        const uint32_t gi = it0 + i;  // ring position of this tile in the CTA's lifetime
-        const int st = gi % kStages;
-        if (gi >= kStages) mbar_wait(&bars->empty[st], ((gi / kStages) - 1) & 1);
-        uint8_t* sk = smem + st * kStageBytes;
-        uint8_t* sv = sk + kKBytes;
-        mbar_arrive_expect_tx(&bars->full[st], kStageBytes);
-        const int t_tile = s_begin + i * kTile;
-        for (int off = 0; off < kTile; off += box_rows) {
-          const int t = t_tile + off;
-          const int page = t / bs;
-          int row = oob_row;
-          if (page < npages) row = (cached ? bars->bt[page - first_page] : bt[page]) * bs + (t % bs);
-          const int x0 = g * kHeadDim;
-          uint8_t* dk = sk + off * 128;
-          uint8_t* dv = sv + off * 128;
-          tma_load_2d_hint(dk, &p.tmap_k, &bars->full[st], x0, row, pol);
-          tma_load_2d_hint(dk + kHalfBytes, &p.tmap_k, &bars->full[st], x0 + 64, row, pol);
-          tma_load_2d_hint(dv, &p.tmap_v, &bars->full[st], x0, row, pol);
-          tma_load_2d_hint(dv + kHalfBytes, &p.tmap_v, &bars->full[st], x0 + 64, row, pol);
-        }
+  __syncwarp();
+  if (lane == 0) {
+    tma_prefetch_desc(&p.tmap_k);
+    tma_prefetch_desc(&p.tmap_v);
+    const int box_rows = bs < kTile ? bs : kTile;
+    const int oob_row = p.num_blocks * bs;  // fully out of range -> zero fill
+    const uint64_t pol = policy_evict_first();
+    for (int i = 0; i < ntiles; ++i) {
+      const uint32_t gi = it0 + i;  // ring position of this tile in the CTA's lifetime
+      const int st = gi % NS;
+      if (gi >= NS) mbar_wait(&empty[st], ((gi / NS) - 1) & 1);
+      uint8_t* sk = smem + st * kStageBytes;
+      uint8_t* sv = sk + kKBytes;
+      mbar_arrive_expect_tx(&full[st], kStageBytes);
+      const int t_tile = s_begin + i * kTile;
+      for (int off = 0; off < kTile; off += box_rows) {
+        const int t = t_tile + off;
+        const int page = t / bs;
+        int row = oob_row;
+        if (page < npages) row = (cached ? bt_smem[page - first_page] : bt[page]) * bs + (t % bs);
+        const int x0 = g * kHeadDim;
+        uint8_t* dk = sk + off * 128;
+        uint8_t* dv = sv + off * 128;
+        tma_load_2d_hint(dk, &p.tmap_k, &full[st], x0, row, pol);
+        tma_load_2d_hint(dk + kHalfBytes, &p.tmap_k, &full[st], x0 + 64, row, pol);
+        tma_load_2d_hint(dv, &p.tmap_v, &full[st], x0, row, pol);
+        tma_load_2d_hint(dv + kHalfBytes, &p.tmap_v, &full[st], x0 + 64, row, pol);
       }
     }
-    return ntiles;
   }
+}
 
-  // -------------------------------------------------------------- consumers
-  const int gq = lane >> 2;  // fragment row group (0..7)
-  const int tq = lane & 3;   // thread in quad
-
-  // Q A-fragments: rows gq and gq+8, 8 k-steps over the 128 dims.
-  uint32_t qa[8][4];
+// Q A-fragments of this thread (rows gq and gq+8, 8 k-steps over the 128
+// dims), from the query tensor or, when q_rows is given, from a copy of the
+// item's nrows query rows ([row][128], 16-bit) in shared memory.
+__device__ __forceinline__ void load_q_frags(const PagedAttnLaunch& p, const uint16_t* q_rows, int nrows, int tok0,
+                                             int g, uint32_t (&qa)[8][4]) {
+  const int lane = threadIdx.x & 31;
+  const int gq = lane >> 2;
+  const int tq = lane & 3;
   {
     const uint16_t* q = static_cast<const uint16_t*>(p.query);
     const int rows[2] = {gq, gq + 8};
@@ -207,7 +156,8 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
       }
       if (r < nrows) {
         const int t = tok0 + r / p.group, h = g * p.group + r % p.group;
-        const uint16_t* src = q + (static_cast<size_t>(t) * p.num_heads + h) * kHeadDim;
+        const uint16_t* src =
+            q_rows != nullptr ? q_rows + r * kHeadDim : q + (static_cast<size_t>(t) * p.num_heads + h) * kHeadDim;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           v[ri][ks][0] = *reinterpret_cast<const uint32_t*>(src + ks * 16 + 2 * tq);
@@ -223,12 +173,26 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
       qa[ks][3] = v[1][ks][1];
     }
   }
+}
 
-  float o[16][4];
+// Consumer warps of one item: the item's tiles from the ring (positions
+// it0, it0 + 1, ...) against the Q fragments qa; leaves this thread's O fragments, row
+// maxima (log2 units) and quad-reduced row sums.
+template <bool kFp16, int NS>
+__device__ __forceinline__ void consume_tiles(const PagedAttnLaunch& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                              uint32_t it0, int ntiles, int s_begin, int s_end,
+                                              const uint32_t (&qa)[8][4], float (&o)[16][4], float& m0, float& m1,
+                                              float& l0, float& l1) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tq = lane & 3;  // thread in quad
+
 #pragma unroll
   for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY;  // running max (log2 units) rows gq, gq+8
-  float l0 = 0.f, l1 = 0.f;              // this thread's share of the row sums
+  m0 = -INFINITY;  // running max (log2 units) rows gq, gq+8
+  m1 = -INFINITY;
+  l0 = 0.f;        // this thread's share of the row sums
+  l1 = 0.f;
 
   const uint32_t smem_base = smem_u32(smem);
   const int wrow = warp * 16;  // this warp's first token row within a tile
@@ -237,8 +201,8 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
 
   for (int i = 0; i < ntiles; ++i) {
     const uint32_t gi = it0 + i;
-    const int st = gi % kStages;
-    mbar_wait(&bars->full[st], (gi / kStages) & 1);
+    const int st = gi % NS;
+    mbar_wait(&full[st], (gi / NS) & 1);
     const uint32_t kbase = smem_base + st * kStageBytes;
     const uint32_t vbase = kbase + kKBytes;
 
@@ -320,7 +284,7 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&bars->empty[st]);
+    if (lane == 0) mbar_arrive(&empty[st]);
   }
 
   // row sums over the quad
@@ -328,16 +292,26 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+}
 
-  // --------------------------------------------- merge the 4 warps in smem
-  // All tiles are consumed (every full barrier was waited by every warp), so
-  // the stage ring is free once all consumer warps reach this barrier.
+// Merge of the 4 consumer warps' (m, l, O) through shared memory at
+// merge_smem (kMergeBytes), then the item's output: a split partial (O, LSE)
+// or, for a single split, the final O and LSE.
+constexpr int kSoStride = kHeadDim + 8;
+constexpr int kMergeBytes = (kConsumerWarps * 16 * kSoStride + 2 * kConsumerWarps * 16) * 4;
+template <bool kFp16>
+__device__ __forceinline__ void merge_store(const PagedAttnLaunch& p, float* merge_smem, const float (&o)[16][4],
+                                            float m0, float m1, float l0, float l1, int nrows, int tok0, int g,
+                                            int split) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int gq = lane >> 2;
+  const int tq = lane & 3;
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
   // Rows are padded to 136 floats: the 8 rows of one fragment store then fall
   // on distinct banks (row r starts at bank 8r mod 32), and only the query
   // rows that exist are written.
-  constexpr int kSoStride = kHeadDim + 8;
-  float* so = reinterpret_cast<float*>(smem);                 // [4][16][kSoStride]
+  float* so = merge_smem;                                      // [4][16][kSoStride]
   float* sm = so + kConsumerWarps * 16 * kSoStride;           // [4][16]
   float* sl = sm + kConsumerWarps * 16;                       // [4][16]
   if (gq < nrows) {
@@ -399,9 +373,87 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
       for (int cc = c; cc < p.lse_stride; cc += kHeadDim / 4) p.lse[row * p.lse_stride + cc] = lse_nat;
     }
   }
-  return ntiles;
 }
 
+// One (split, kv head, request) item. `it0` = tiles this CTA consumed in
+// earlier items (the ring's barrier phases continue across items);
+// `init_bars` initialises the ring barriers first (one item per CTA). Returns
+// the tiles consumed. All 160 threads call it; on return every tile of the
+// item has landed and the ring's shared memory is free again only after a
+// CTA barrier (the merge reuses it).
+template <bool kFp16>
+__device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8_t* smem, DecodeBarriers* bars,
+                                                 int split, int g, int b, uint32_t it0, bool init_bars) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // The split's block-table entries do not depend on the kv length: the
+  // producer warp issues their load first, so it overlaps the length load.
+  const int s_begin = split * p.split_tokens;
+  const int first_page = s_begin / p.block_size;
+  const int bt_avail = min(kBtCache, p.block_cols - first_page);
+  int bt_pre0 = 0, bt_pre1 = 0;
+  if (warp == kConsumerWarps) {
+    const int32_t* btrow = p.block_table + static_cast<size_t>(b) * p.block_cols + first_page;
+    if (lane < bt_avail) bt_pre0 = btrow[lane];
+    if (lane + 32 < bt_avail) bt_pre1 = btrow[lane + 32];
+  }
+
+  // kv is clamped to the block table's capacity, so no entry past a row is read
+  const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
+  const int q_len = p.q_seqlen_value > 0 ? p.q_seqlen_value : static_cast<int>(p.q_seqlens[b]);
+  const int nrows = q_len * p.group;
+  const int tok0 = request_token_offset(p, b);
+  const int s_end = min(kv, s_begin + p.split_tokens);
+  const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
+
+  // Empty split (kv shorter than this split's start, or no query rows):
+  // write -inf partials so the combine step skips it.
+  if (ntiles == 0 || nrows == 0) {
+    if (p.num_splits > 1 || p.partial_out) {
+      for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
+        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+        p.part_lse[static_cast<size_t>(split) * p.num_tokens * p.num_heads + static_cast<size_t>(t) * p.num_heads + h] =
+            -INFINITY;
+      }
+    } else {
+      // single split: kv == 0 -> out = 0, lse = -inf
+      for (int i = threadIdx.x; i < nrows * kHeadDim / 2; i += blockDim.x) {
+        int r = i / (kHeadDim / 2), d = (i % (kHeadDim / 2)) * 2;
+        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+        store_out<kFp16>(p.out, p.out_dtype, (static_cast<size_t>(t) * p.num_heads + h) * kHeadDim + d, 0.f, 0.f);
+      }
+      for (int i = threadIdx.x; i < nrows * p.lse_stride; i += blockDim.x) {
+        int r = i / p.lse_stride, c = i % p.lse_stride;
+        int t = tok0 + r / p.group, h = g * p.group + r % p.group;
+        p.lse[(static_cast<size_t>(t) * p.num_heads + h) * p.lse_stride + c] = -INFINITY;
+      }
+    }
+    return 0;
+  }
+
+  if (init_bars) {
+    if (threadIdx.x == 0) init_decode_barriers(bars);
+    __syncthreads();
+  }
+
+  if (warp == kConsumerWarps) {
+    produce_tiles<kStages>(p, smem, bars->full, bars->empty, bars->bt, b, g, s_begin, s_end, kv, ntiles, it0, bt_pre0,
+                           bt_pre1);
+    return ntiles;
+  }
+
+  uint32_t qa[8][4];
+  load_q_frags(p, nullptr, nrows, tok0, g, qa);
+  float o[16][4];
+  float m0, m1, l0, l1;
+  consume_tiles<kFp16, kStages>(p, smem, bars->full, bars->empty, it0, ntiles, s_begin, s_end, qa, o, m0, m1, l0, l1);
+  // All tiles are consumed (every full barrier was waited by every warp), so
+  // the stage ring is free for the merge once all consumer warps reach its
+  // first barrier.
+  merge_store<kFp16>(p, reinterpret_cast<float*>(smem), o, m0, m1, l0, l1, nrows, tok0, g, split);
+  return ntiles;
+}
 __device__ __forceinline__ uint8_t* decode_smem() {
   extern __shared__ uint8_t smem_raw[];
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -417,27 +469,69 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
   if (p.pdl && threadIdx.x == 0) pdl_wait();
 }
 
-// Planned form for wide ragged batches: decode_plan_kernel (launched just
-// before, this kernel being its programmatic dependent) lists the non-empty
-// (request, split) items; gridDim.x CTAs per kv head (two per SM in all) take
-// items from a per-kv-head counter, and first write -inf partial LSEs for the
-// empty split slots of the requests b = blockIdx.x (mod gridDim.x), so the
-// combine sees every slot. No CTA is launched for an empty split.
+// Streaming form of the planned decode, three roles:
+//   warp 5 (fetcher) takes the items (per-kv-head counter) and prepares each
+//     in one of two shared-memory slots: the item code, its kv length, the
+//     split's block-table entries and the item's query rows;
+//   warp 4 (producer) streams each slot's tiles into a 2-stage ring whose
+//     positions continue across items;
+//   warps 0-3 (consumers) take Q from the slot, consume the tiles and merge
+//     through their own shared-memory area.
+// The ring never drains between items and no role waits on a global load
+// at an item boundary: the next item's metadata and rows arrive while the
+// current one streams. A slot is free again once the producer has issued its
+// tiles and every consumer warp has read its Q. Two CTAs per SM.
+constexpr int kSStages = 2;
+constexpr int kStreamThreads = kThreads + 32;
+
+struct __align__(16) StreamSlot {
+  int32_t code;  // (b << 8) | split, or -1: no more items
+  int32_t kv;
+  int32_t pad[2];
+  int32_t bt[kBtCache];
+  uint16_t q[16 * kHeadDim];  // the item's <= 16 query rows
+};
+
+struct __align__(16) StreamBarriers {
+  uint64_t full[kSStages];
+  uint64_t empty[kSStages];
+  uint64_t item_full[2];   // slot written (32 fetcher lanes)
+  uint64_t item_empty[2];  // slot consumed (producer + one arrive per consumer warp)
+  StreamSlot slot[2];
+};
+
+constexpr int kStreamSmemBytes = kSStages * kStageBytes + kMergeBytes + 1024 /*align*/ +
+                                 static_cast<int>(sizeof(StreamBarriers));
+
 template <bool kFp16>
-__global__ void __launch_bounds__(kThreads, 2) paged_decode_planned_kernel(const __grid_constant__ PagedAttnLaunch p) {
+__global__ void __launch_bounds__(kStreamThreads, 2)
+    paged_decode_stream_kernel(const __grid_constant__ PagedAttnLaunch p) {
   pdl_launch_dependents();
   uint8_t* smem = decode_smem();
-  DecodeBarriers* bars = reinterpret_cast<DecodeBarriers*>(smem + kStages * kStageBytes);
-  __shared__ int32_t sh_item;
+  float* merge_smem = reinterpret_cast<float*>(smem + kSStages * kStageBytes);
+  StreamBarriers* bars = reinterpret_cast<StreamBarriers*>(smem + kSStages * kStageBytes + kMergeBytes);
   const int g = blockIdx.y;
-  if (threadIdx.x == 0) init_decode_barriers(bars);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], kConsumerWarps);
+    }
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&bars->item_full[q], 32);
+      mbar_init(&bars->item_empty[q], 1 + kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
   pdl_wait();  // the item list, its count and the zeroed counters are complete
   __syncthreads();
   const size_t plane = static_cast<size_t>(p.num_tokens) * p.num_heads;
+  const int nrows = p.q_seqlen_value * p.group;
+  const int cap = p.block_cols * p.block_size;
   for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
-    const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
+    const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(cap)));
     const int used = kv > 0 ? min(p.num_splits, (kv + p.split_tokens - 1) / p.split_tokens) : 0;
-    const int nrows = p.q_seqlen_value * p.group;
     const int tok0 = b * p.q_seqlen_value;
     for (int i = threadIdx.x; i < (p.num_splits - used) * nrows; i += blockDim.x) {
       const int s = used + i / nrows, r = i % nrows;
@@ -445,16 +539,83 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_planned_kernel(const
       p.part_lse[static_cast<size_t>(s) * plane + static_cast<size_t>(t) * p.num_heads + h] = -INFINITY;
     }
   }
-  const int count = *p.plan_count;
-  uint32_t it0 = 0;
-  for (;;) {
-    if (threadIdx.x == 0) sh_item = atomicAdd(p.plan_counters + g, 1);
-    __syncthreads();
-    const int item = sh_item;
-    if (item >= count) break;
-    const int32_t code = p.plan_items[item];
-    it0 += paged_decode_item<kFp16>(p, smem, bars, code & 0xFF, g, code >> 8, it0, false);
-    __syncthreads();  // the merge used the ring; the next item's loads may start
+  uint32_t it0 = 0;  // ring position of the next tile
+  if (warp == kConsumerWarps + 1) {
+    // ------------------------------------------------------------- fetcher
+    const int count = *p.plan_count;
+    for (int j = 0;; ++j) {
+      const int q = j & 1;
+      StreamSlot& sl = bars->slot[q];
+      if (j >= 2) mbar_wait(&bars->item_empty[q], ((j >> 1) - 1) & 1);
+      int item = 0;
+      if (lane == 0) item = atomicAdd(p.plan_counters + g, 1);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      const int code = item < count ? p.plan_items[item] : -1;
+      if (code >= 0) {
+        const int split = code & 0xFF, b = code >> 8;
+        const int first_page = split * p.split_tokens / p.block_size;
+        const int bt_avail = min(kBtCache, p.block_cols - first_page);
+        const int32_t* btrow = p.block_table + static_cast<size_t>(b) * p.block_cols + first_page;
+        static_assert(kBtCache <= 64, "two block-table entries per lane");
+        if (lane < bt_avail) sl.bt[lane] = btrow[lane];
+        if (lane + 32 < bt_avail) sl.bt[lane + 32] = btrow[lane + 32];
+        if (lane == 0) sl.kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(cap)));
+        // query rows: nrows x 256 bytes as 16-byte chunks over the warp
+        const uint4* qsrc = static_cast<const uint4*>(p.query);
+        uint4* qdst = reinterpret_cast<uint4*>(sl.q);
+        for (int c = lane; c < nrows * (kHeadDim / 8); c += 32) {
+          const int r = c / (kHeadDim / 8), w = c % (kHeadDim / 8);
+          const int t = b * p.q_seqlen_value + r / p.group, h = g * p.group + r % p.group;
+          qdst[c] = qsrc[(static_cast<size_t>(t) * p.num_heads + h) * (kHeadDim / 8) + w];
+        }
+      }
+      if (lane == 0) sl.code = code;
+      mbar_arrive(&bars->item_full[q]);  // each lane releases its own stores
+      if (code < 0) break;
+    }
+  } else if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    for (int j = 0;; ++j) {
+      const int q = j & 1;
+      StreamSlot& sl = bars->slot[q];
+      mbar_wait(&bars->item_full[q], (j >> 1) & 1);
+      const int code = sl.code;
+      if (code < 0) break;
+      const int split = code & 0xFF, b = code >> 8;
+      const int s_begin = split * p.split_tokens;
+      const int kv = sl.kv;
+      const int s_end = min(kv, s_begin + p.split_tokens);
+      const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
+      produce_tiles<kSStages, true>(p, smem, bars->full, bars->empty, sl.bt, b, g, s_begin, s_end, kv, ntiles, it0, 0,
+                                    0);
+      __syncwarp();  // lane 0 has issued every tile: the slot's entries are no longer read
+      if (lane == 0) mbar_arrive(&bars->item_empty[q]);
+      it0 += ntiles;
+    }
+  } else {
+    // ----------------------------------------------------------- consumers
+    for (int j = 0;; ++j) {
+      const int q = j & 1;
+      StreamSlot& sl = bars->slot[q];
+      mbar_wait(&bars->item_full[q], (j >> 1) & 1);
+      const int code = sl.code;
+      if (code < 0) break;
+      const int split = code & 0xFF, b = code >> 8;
+      const int s_begin = split * p.split_tokens;
+      const int s_end = min(sl.kv, s_begin + p.split_tokens);
+      const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
+      const int tok0 = b * p.q_seqlen_value;
+      uint32_t qa[8][4];
+      load_q_frags(p, sl.q, nrows, tok0, g, qa);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->item_empty[q]);
+      float o[16][4];
+      float m0, m1, l0, l1;
+      consume_tiles<kFp16, kSStages>(p, smem, bars->full, bars->empty, it0, ntiles, s_begin, s_end, qa, o, m0, m1, l0,
+                                     l1);
+      merge_store<kFp16>(p, merge_smem, o, m0, m1, l0, l1, nrows, tok0, g, split);
+      it0 += ntiles;
+    }
   }
 }
 
@@ -558,11 +719,12 @@ cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_
     launch_maybe_pdl(decode_plan_kernel, dim3(1), dim3(1024), 0, stream, p.pdl != 0, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    auto kern = fp16 ? paged_decode_planned_kernel<true> : paged_decode_planned_kernel<false>;
-    e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
+    auto kern = fp16 ? paged_decode_stream_kernel<true> : paged_decode_stream_kernel<false>;
+    e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kStreamSmemBytes);
     if (e != cudaSuccess) return e;
     const int per_head = std::max(1, (2 * kNumSMs) / std::max(1, p.kv_heads));
-    return launch_maybe_pdl(kern, dim3(per_head, p.kv_heads, 1), dim3(kThreads), kSmemBytes, stream, true, p);
+    return launch_maybe_pdl(kern, dim3(per_head, p.kv_heads, 1), dim3(kStreamThreads), kStreamSmemBytes, stream, true,
+                            p);
   }
   dim3 grid(p.num_splits, p.kv_heads, p.batch);
   auto kern = fp16 ? paged_decode_kernel<true> : paged_decode_kernel<false>;
