@@ -146,24 +146,25 @@ def test_suffix_decode_block_sizes(dtype, bs):
     assert np.abs(l[~z] - l_ref[~z]).max() < LSE_TOL
 
 
-@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
-def test_planned_suffix_decode_wide_ragged(dtype):
+@pytest.mark.parametrize("q_len,H,dtype", [(1, 16, "bf16"), (1, 16, "fp16"), (2, 40, "fp16"), (4, 32, "bf16")])
+def test_planned_suffix_decode_wide_ragged(q_len, H, dtype):
     """A wide ragged batch (512 requests x 8 kv heads, block size 16, lengths
     from 0 to 4000, most short: 8 splits x 4096 pairs > 16384 slots) takes
     the planned decode: the device lists only the non-empty (request, split)
     items and the empty split slots get -inf partials. Same gates as the
-    per-item decode, with and without the combine (partials only)."""
+    per-item decode, with and without the combine (partials only); 2, 10
+    and 16 query rows per (request, kv head) (the item slot's Q rows)."""
     import torch
     Hh.need_cuda()
     rng = np.random.default_rng(11)
     kv = np.clip(rng.lognormal(np.log(150), 1.0, 512), 1, 4000).astype(int)
     kv[rng.random(512) < 0.1] = 0
     kv[:3] = [4000, 1025, 512]
-    dev, host = _rand_case(512, 16, 8, 16, list(kv), 1, dtype, seed=21)
+    dev, host = _rand_case(512, H, 8, 16, list(kv), q_len, dtype, seed=21 + q_len)
     C = Hh.capi()
-    plan = C.plan(C.paged_desc(*dev, 1), 1, True)
+    plan = C.plan(C.paged_desc(*dev, q_len), q_len, True)
     assert plan.kernel == 2 and plan.split_tokens == 512 and plan.num_splits == 8
-    out, lse = Hh.run_capi_paged(*dev, 1, suffix=True)
+    out, lse = Hh.run_capi_paged(*dev, q_len, suffix=True)
     qf, kf, vf, bt, qs, kvs = host
     seg = lambda n: O.decode_segments(n, split=512, tile=64, warps=4)
     o_ks, l_ks, A = O.paged_attention_ref(qf, kf, vf, bt, qs, kvs, segments=seg, p_dtype=dtype,
@@ -171,18 +172,19 @@ def test_planned_suffix_decode_wide_ragged(dtype):
     o = Hh.dev_to_f64(out)
     l = Hh.dev_to_f64(lse).reshape(o_ks.shape[:2])
     half_ulp = 0.5 * np.maximum(O.ulp(o_ks, dtype), O.ulp(o, dtype))
-    _assert_within(o, o_ks, A + half_ulp + 3e-6, kvs)
-    z = kvs == 0
+    kv_tok = np.repeat(kvs, q_len)  # per query token
+    _assert_within(o, o_ks, A + half_ulp + 3e-6, kv_tok)
+    z = kv_tok == 0
     assert np.all(np.isneginf(l[z])) and np.all(o[z] == 0)
     assert np.abs(l[~z] - l_ks[~z]).max() < 1e-5
     # partials only: slot s of a request holds its split s (or -inf beyond its length)
-    d = C.paged_desc(*dev, 1, flags=C.FLAG_PARTIALS_ONLY)
+    d = C.paged_desc(*dev, q_len, flags=C.FLAG_PARTIALS_ONLY)
     ws = torch.full((C.suffix_workspace_size(d),), 0x7F, dtype=torch.uint8, device="cuda")
     C.suffix_decode(d, None, None, ws)
     torch.cuda.synchronize()
     assert C.device_error() == 0
-    rows = 512 * 16
-    part_lse = ws[8 * 4 * rows * 128:8 * 4 * rows * 129].view(torch.float32).view(8, 512, 16).cpu().numpy()
+    rows = 512 * q_len * H
+    part_lse = ws[8 * 4 * rows * 128:8 * 4 * rows * 129].view(torch.float32).view(8, 512, q_len * H).cpu().numpy()
     used = np.minimum(8, -(-kvs // 512))
     for s in range(8):
         assert np.all(np.isneginf(part_lse[s][s >= used])), s
