@@ -309,6 +309,217 @@ cudaError_t launch_bn(const GateUpLaunch& L, const void* a, const void* b, cudaS
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair form for SwiGLU over 129..256 rows: a cluster of two CTAs computes
+// a 256-row x 256-column output tile with tcgen05.mma.cta_group::2 (M = 256,
+// N = 256, issued by rank 0). Per K block each CTA loads its own 128 rows of X
+// and 256 rows of W -- rank 0 the gate rows [n0, n0+256), rank 1 the up rows
+// [I+n0, I+n0+256) -- so one pair instruction on the first 128 of each CTA's
+// W rows yields gate | up of output columns [n0, n0+128) for all 256 rows,
+// and a second one on the next 128 rows those of [n0+128, n0+256). Each CTA
+// holds its 128 rows of both accumulators (2 x 256 TMEM columns) and runs the
+// SwiGLU epilogue on them. Per CTA this moves 48 KB per K block for 128 x 512
+// accumulator outputs, against 64 KB for 256 x 256 in the one-CTA 256-row
+// form: a quarter less operand traffic through L2 for the same MMA work.
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 4;
+constexpr int kPairABytes = kBM * kBK * 2;                  // 16 KB: this CTA's X rows
+constexpr int kPairBBytes = 2 * 128 * kBK * 2;              // 32 KB: this CTA's 256 W rows
+constexpr int kPairStageBytes = kPairABytes + kPairBBytes;  // 48 KB
+constexpr int kPairStagingOff = kPairStages * kPairStageBytes;
+constexpr int kPairStagingBytes = kBM * 128 * 2;            // [128 rows x 128 cols] bf16, two SW128 halves
+constexpr int kPairBarOff = kPairStagingOff + kPairStagingBytes;
+constexpr int kPairSmem = kPairBarOff + 256 + 1024;
+static_assert(kPairSmem <= 227 * 1024, "shared memory budget");
+
+struct __align__(8) PairBars {
+  uint64_t full[kPairStages];   // rank 0's: both CTAs' loads of a stage
+  uint64_t empty[kPairStages];  // each CTA's: the pair's MMAs read the stage
+  uint64_t acc_full;            // each CTA's: the tile's MMAs are done
+  uint64_t acc_empty;           // rank 0's: both CTAs' epilogues read TMEM
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_constant__ GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_cta_rank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int num_tiles = p.num_n;  // 256-column tiles; M <= 256 is one row tile
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 2);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // barriers and TMEM of both CTAs are ready
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
+      int it = 0;
+      for (int tile = cluster; tile < num_tiles; tile += nclusters) {
+        const int wrow = (rank == 0 ? 0 : p.I) + tile * 256;  // gate rows (rank 0) or up rows (rank 1)
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int st = it % kPairStages;
+          if (it >= kPairStages) mbar_wait_cluster(&bars->empty[st], ((it / kPairStages) - 1) & 1);
+          const uint32_t full_l = mapa_shared(smem_u32(&bars->full[st]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[st], 2 * kPairStageBytes);
+          uint8_t* sa = smem + st * kPairStageBytes;
+          uint8_t* sb = sa + kPairABytes;
+          tma_load_2d_pair(sa, &p.tm_a, full_l, kb * kBK, static_cast<int>(rank) * kBM);
+          tma_load_2d_pair(sb, &p.tm_b, full_l, kb * kBK, wrow);
+          tma_load_2d_pair(sb + 128 * 128, &p.tm_b, full_l, kb * kBK, wrow + 128);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = make_idesc_f16(256, 256, 1, 0, 0);
+      int it = 0, tc = 0;
+      for (int tile = cluster; tile < num_tiles; tile += nclusters, ++tc) {
+        if (tc > 0) mbar_wait_cluster(&bars->acc_empty, (tc - 1) & 1);
+        tc_fence_after();
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int st = it % kPairStages;
+          mbar_wait_cluster(&bars->full[st], (it / kPairStages) & 1);
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + st * kPairStageBytes);
+          const uint32_t b0 = a0 + kPairABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = make_smem_desc(a0 + k * 32, 16, 1024, 2);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_f16_ss_pair(tbase, ad, make_smem_desc(b0 + k * 32, 16, 1024, 2), idesc, acc);
+            umma_f16_ss_pair(tbase + 256, ad, make_smem_desc(b0 + 128 * 128 + k * 32, 16, 1024, 2), idesc, acc);
+          }
+          umma_commit_pair(&bars->empty[st], 3);
+        }
+        umma_commit_pair(&bars->acc_full, 3);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int etid = threadIdx.x - 64;
+    const uint32_t acc_empty_l = mapa_shared(smem_u32(&bars->acc_empty), 0);
+    uint8_t* stg = smem + kPairStagingOff;
+    int tc = 0;
+    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++tc) {
+      mbar_wait_cluster(&bars->acc_full, tc & 1);
+      tc_fence_after();
+      const int m0 = static_cast<int>(rank) * kBM;
+      for (int h = 0; h < 2; ++h) {
+        const int n0 = tile * 256 + h * 128;
+        const uint32_t acc = tbase + lane_off + h * 256;
+        if (etid == 0) bulk_wait_group_read0();   // the staging buffer's previous stores have read it
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+        for (int c = 0; c < 128 / 16; ++c) {
+          uint32_t g[16], u[16];
+          tmem_ld_32x32b_x16(acc + c * 16, g);
+          tmem_ld_32x32b_x16(acc + 128 + c * 16, u);
+          tmem_wait_ld();
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            pk[e >> 1] = pack2<false>(silu_mul(__uint_as_float(g[e]), __uint_as_float(u[e])),
+                                      silu_mul(__uint_as_float(g[e + 1]), __uint_as_float(u[e + 1])));
+          }
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int ch = c * 2 + hh;
+            *reinterpret_cast<uint4*>(stg + (ch >> 3) * (kBM * 128) + sw128(r, ch & 7)) =
+                make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (etid == 0) {
+          // this CTA's TMEM reads of the tile are done after the second half
+          if (h == 1) mbar_arrive_remote(acc_empty_l);
+          tma_store_2d(&p.tm_d, stg, n0, m0);
+          tma_store_2d(&p.tm_d, stg + kBM * 128, n0 + 64, m0);
+          bulk_commit_group();
+        }
+      }
+    }
+    if (etid == 0) bulk_wait_group0();
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // no MMA of the pair still writes either CTA's TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 512);
+  }
+}
+
+cudaError_t launch_pair(const GateUpLaunch& L, const void* a, const void* b, cudaStream_t stream) {
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = L.M;
+  p.K = L.K;
+  p.I = L.I;
+  p.num_m = 1;
+  p.num_n = L.I / 256;
+  p.num_kb = (L.K + kBK - 1) / kBK;
+  p.mode = L.mode;
+  if (!enc(&p.tm_a, a, L.K, L.M, static_cast<uint64_t>(L.K) * 2, kBM)) return cudaErrorInvalidValue;
+  if (!enc(&p.tm_b, b, L.K, 2ull * L.I, static_cast<uint64_t>(L.K) * 2, 128)) return cudaErrorInvalidValue;
+  if (!enc(&p.tm_d, L.d, L.I, L.M, static_cast<uint64_t>(L.d_stride) * 2, kBM)) return cudaErrorInvalidValue;
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gateup_pair_kernel), kPairSmem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // persistent: as many pairs as can be resident at once (per device), at
+  // most one per tile
+  static int max_clusters[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& mc = max_clusters[dev & 63];
+  if (mc == 0) {
+    cfg.gridDim = dim3(kNumSMs);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(gateup_pair_kernel), &cfg) != cudaSuccess ||
+        n <= 0) {
+      cudaGetLastError();
+      n = kNumSMs / 2;
+    }
+    mc = std::min(n, kNumSMs / 2);
+  }
+  cfg.gridDim = dim3(2 * std::min(p.num_n, mc));
+  return cudaLaunchKernelEx(&cfg, gateup_pair_kernel, p);
+}
+
+// ---------------------------------------------------------------------------
 // Small-M variant (M <= 128, the weight-streaming regime): swap the operands so
 // the paired weight tile fills the 128-row MMA side. D^T[128 x MP] =
 // W_tile[128 x K] X^T[K x MP], W_tile = gate rows [n0, n0+64) followed by the
@@ -504,7 +715,11 @@ cudaError_t launch_gateup(const GateUpLaunch& L, const void* a, const void* b, c
     if (best < 0)
       for (int c = 0; c < 3; ++c)
         if (cand[c] > 0 && (best < 0 || cand[c] < cand[best])) best = c;
-    if (best == 0) return launch_bn<128, 2>(L, a, b, stream);
+    if (best == 0) {
+      // SwiGLU with 256-column pair tiles (the same CTA count): the CTA-pair form
+      if (L.mode == 1 && L.M > kBM && L.I % 256 == 0) return launch_pair(L, a, b, stream);
+      return launch_bn<128, 2>(L, a, b, stream);
+    }
     if (best == 2) return launch_bn<64, 1>(L, a, b, stream);
   }
   return launch_bn<128>(L, a, b, stream);
