@@ -310,26 +310,33 @@ cudaError_t launch_bn(const GateUpLaunch& L, const void* a, const void* b, cudaS
 
 // ---------------------------------------------------------------------------
 // CTA-pair form for SwiGLU over 129..256 rows: a cluster of two CTAs computes
-// a 256-row x 256-column output tile with tcgen05.mma.cta_group::2 (M = 256,
-// N = 256, issued by rank 0). Per K block each CTA loads its own 128 rows of X
-// and 256 rows of W -- rank 0 the gate rows [n0, n0+256), rank 1 the up rows
-// [I+n0, I+n0+256) -- so one pair instruction on the first 128 of each CTA's
-// W rows yields gate | up of output columns [n0, n0+128) for all 256 rows,
-// and a second one on the next 128 rows those of [n0+128, n0+256). Each CTA
-// holds its 128 rows of both accumulators (2 x 256 TMEM columns) and runs the
-// SwiGLU epilogue on them. Per CTA this moves 48 KB per K block for 128 x 512
-// accumulator outputs, against 64 KB for 256 x 256 in the one-CTA 256-row
-// form: a quarter less operand traffic through L2 for the same MMA work.
+// a 256-row x 2C-column output tile (C = 128 or 112) with
+// tcgen05.mma.cta_group::2 (M = 256, N = 2C, issued by rank 0). Per K block
+// each CTA loads its own 128 rows of X and 2C rows of W -- rank 0 the gate
+// rows [n0, n0+2C), rank 1 the up rows [I+n0, I+n0+2C) -- so one pair
+// instruction on the first C of each CTA's W rows yields gate | up of output
+// columns [n0, n0+C) for all 256 rows, and a second one on the next C rows
+// those of [n0+C, n0+2C). Each CTA holds its 128 rows of both accumulators
+// (2 x 2C TMEM columns) and runs the SwiGLU epilogue on them. With C = 128 a
+// CTA moves 48 KB per K block for 128 x 512 accumulator outputs, against
+// 64 KB for 256 x 256 in the one-CTA 256-row form; C = 112 trades a little of
+// that for tile counts that fit the SMs (I = 14336: 128 CTAs instead of 112).
 // ---------------------------------------------------------------------------
+template <int C>
+struct PairCfg {
+  static_assert(C == 128 || C == 112, "pair tile: 2 x 128 or 2 x 112 output columns");
+  static constexpr int kStages = 4;
+  static constexpr int kABytes = kBM * kBK * 2;             // 16 KB: this CTA's X rows
+  static constexpr int kBHalf = C * kBK * 2;                // one MMA's W rows of this CTA
+  static constexpr int kStageBytes = kABytes + 2 * kBHalf;  // 48 KB (C = 128) / 44 KB (C = 112)
+  static constexpr int kStagingOff = kStages * kStageBytes;
+  static constexpr int kStagingBytes = kBM * C * 2;         // [128 rows x C cols] bf16
+  static constexpr int kBarOff = kStagingOff + kStagingBytes;
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static_assert(kSmem <= 227 * 1024, "shared memory budget");
+  static_assert(kBHalf % 1024 == 0, "the second W block starts on a swizzle atom");
+};
 constexpr int kPairStages = 4;
-constexpr int kPairABytes = kBM * kBK * 2;                  // 16 KB: this CTA's X rows
-constexpr int kPairBBytes = 2 * 128 * kBK * 2;              // 32 KB: this CTA's 256 W rows
-constexpr int kPairStageBytes = kPairABytes + kPairBBytes;  // 48 KB
-constexpr int kPairStagingOff = kPairStages * kPairStageBytes;
-constexpr int kPairStagingBytes = kBM * 128 * 2;            // [128 rows x 128 cols] bf16, two SW128 halves
-constexpr int kPairBarOff = kPairStagingOff + kPairStagingBytes;
-constexpr int kPairSmem = kPairBarOff + 256 + 1024;
-static_assert(kPairSmem <= 227 * 1024, "shared memory budget");
 
 struct __align__(8) PairBars {
   uint64_t full[kPairStages];   // rank 0's: both CTAs' loads of a stage
@@ -339,14 +346,16 @@ struct __align__(8) PairBars {
   uint32_t tmem_base;
 };
 
+template <int C>
 __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_constant__ GemmParams p) {
+  using Cfg = PairCfg<C>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairBarOff);
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + Cfg::kBarOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_cta_rank();
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
-  const int num_tiles = p.num_n;  // 256-column tiles; M <= 256 is one row tile
+  const int num_tiles = p.num_n;  // 2C-column tiles; M <= 256 is one row tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
@@ -373,23 +382,23 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
       tma_prefetch_desc(&p.tm_b);
       int it = 0;
       for (int tile = cluster; tile < num_tiles; tile += nclusters) {
-        const int wrow = (rank == 0 ? 0 : p.I) + tile * 256;  // gate rows (rank 0) or up rows (rank 1)
+        const int wrow = (rank == 0 ? 0 : p.I) + tile * 2 * C;  // gate rows (rank 0) or up rows (rank 1)
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int st = it % kPairStages;
           if (it >= kPairStages) mbar_wait_cluster(&bars->empty[st], ((it / kPairStages) - 1) & 1);
           const uint32_t full_l = mapa_shared(smem_u32(&bars->full[st]), 0);
-          if (rank == 0) mbar_arrive_expect_tx(&bars->full[st], 2 * kPairStageBytes);
-          uint8_t* sa = smem + st * kPairStageBytes;
-          uint8_t* sb = sa + kPairABytes;
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[st], 2 * Cfg::kStageBytes);
+          uint8_t* sa = smem + st * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kABytes;
           tma_load_2d_pair(sa, &p.tm_a, full_l, kb * kBK, static_cast<int>(rank) * kBM);
           tma_load_2d_pair(sb, &p.tm_b, full_l, kb * kBK, wrow);
-          tma_load_2d_pair(sb + 128 * 128, &p.tm_b, full_l, kb * kBK, wrow + 128);
+          tma_load_2d_pair(sb + Cfg::kBHalf, &p.tm_b, full_l, kb * kBK, wrow + C);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = make_idesc_f16(256, 256, 1, 0, 0);
+      const uint32_t idesc = make_idesc_f16(256, 2 * C, 1, 0, 0);
       int it = 0, tc = 0;
       for (int tile = cluster; tile < num_tiles; tile += nclusters, ++tc) {
         if (tc > 0) mbar_wait_cluster(&bars->acc_empty, (tc - 1) & 1);
@@ -398,14 +407,14 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
           const int st = it % kPairStages;
           mbar_wait_cluster(&bars->full[st], (it / kPairStages) & 1);
           tc_fence_after();
-          const uint32_t a0 = smem_u32(smem + st * kPairStageBytes);
-          const uint32_t b0 = a0 + kPairABytes;
+          const uint32_t a0 = smem_u32(smem + st * Cfg::kStageBytes);
+          const uint32_t b0 = a0 + Cfg::kABytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = make_smem_desc(a0 + k * 32, 16, 1024, 2);
             const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
             umma_f16_ss_pair(tbase, ad, make_smem_desc(b0 + k * 32, 16, 1024, 2), idesc, acc);
-            umma_f16_ss_pair(tbase + 256, ad, make_smem_desc(b0 + 128 * 128 + k * 32, 16, 1024, 2), idesc, acc);
+            umma_f16_ss_pair(tbase + 2 * C, ad, make_smem_desc(b0 + Cfg::kBHalf + k * 32, 16, 1024, 2), idesc, acc);
           }
           umma_commit_pair(&bars->empty[st], 3);
         }
@@ -419,22 +428,22 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int etid = threadIdx.x - 64;
     const uint32_t acc_empty_l = mapa_shared(smem_u32(&bars->acc_empty), 0);
-    uint8_t* stg = smem + kPairStagingOff;
+    uint8_t* stg = smem + Cfg::kStagingOff;
     int tc = 0;
     for (int tile = cluster; tile < num_tiles; tile += nclusters, ++tc) {
       mbar_wait_cluster(&bars->acc_full, tc & 1);
       tc_fence_after();
       const int m0 = static_cast<int>(rank) * kBM;
       for (int h = 0; h < 2; ++h) {
-        const int n0 = tile * 256 + h * 128;
-        const uint32_t acc = tbase + lane_off + h * 256;
+        const int n0 = tile * 2 * C + h * C;
+        const uint32_t acc = tbase + lane_off + h * 2 * C;
         if (etid == 0) bulk_wait_group_read0();   // the staging buffer's previous stores have read it
         asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
-        for (int c = 0; c < 128 / 16; ++c) {
+        for (int c = 0; c < C / 16; ++c) {
           uint32_t g[16], u[16];
           tmem_ld_32x32b_x16(acc + c * 16, g);
-          tmem_ld_32x32b_x16(acc + 128 + c * 16, u);
+          tmem_ld_32x32b_x16(acc + C + c * 16, u);
           tmem_wait_ld();
           uint32_t pk[8];
 #pragma unroll
@@ -445,8 +454,9 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int ch = c * 2 + hh;
-            *reinterpret_cast<uint4*>(stg + (ch >> 3) * (kBM * 128) + sw128(r, ch & 7)) =
-                make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
+            // C = 128: two 64-column SW128 halves; C = 112: plain [128][112] rows
+            uint8_t* dst = C == 128 ? stg + (ch >> 3) * (kBM * 128) + sw128(r, ch & 7) : stg + r * (C * 2) + ch * 16;
+            *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
           }
         }
         fence_proxy_async_smem();
@@ -456,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
           // this CTA's TMEM reads of the tile are done after the second half
           if (h == 1) mbar_arrive_remote(acc_empty_l);
           tma_store_2d(&p.tm_d, stg, n0, m0);
-          tma_store_2d(&p.tm_d, stg + kBM * 128, n0 + 64, m0);
+          if (C == 128) tma_store_2d(&p.tm_d, stg + kBM * 128, n0 + 64, m0);
           bulk_commit_group();
         }
       }
@@ -473,20 +483,25 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
   }
 }
 
+template <int C>
 cudaError_t launch_pair(const GateUpLaunch& L, const void* a, const void* b, cudaStream_t stream) {
+  using Cfg = PairCfg<C>;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = L.M;
   p.K = L.K;
   p.I = L.I;
   p.num_m = 1;
-  p.num_n = L.I / 256;
+  p.num_n = L.I / (2 * C);
   p.num_kb = (L.K + kBK - 1) / kBK;
   p.mode = L.mode;
   if (!enc(&p.tm_a, a, L.K, L.M, static_cast<uint64_t>(L.K) * 2, kBM)) return cudaErrorInvalidValue;
-  if (!enc(&p.tm_b, b, L.K, 2ull * L.I, static_cast<uint64_t>(L.K) * 2, 128)) return cudaErrorInvalidValue;
-  if (!enc(&p.tm_d, L.d, L.I, L.M, static_cast<uint64_t>(L.d_stride) * 2, kBM)) return cudaErrorInvalidValue;
-  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gateup_pair_kernel), kPairSmem);
+  if (!enc(&p.tm_b, b, L.K, 2ull * L.I, static_cast<uint64_t>(L.K) * 2, C)) return cudaErrorInvalidValue;
+  // D: C = 128 stores two 64-column SW128 boxes, C = 112 one plain 112-column box
+  if (!encode_tmap_2d(&p.tm_d, L.d, L.I, L.M, static_cast<uint64_t>(L.d_stride) * 2, C == 128 ? 64 : C, kBM, C == 128,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+    return cudaErrorInvalidValue;
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gateup_pair_kernel<C>), Cfg::kSmem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -495,20 +510,21 @@ cudaError_t launch_pair(const GateUpLaunch& L, const void* a, const void* b, cud
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.dynamicSmemBytes = Cfg::kSmem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // persistent: as many pairs as can be resident at once (per device), at
   // most one per tile
-  static int max_clusters[64] = {};
+  static int max_clusters[64] = {};  // per C instantiation
   int dev = 0;
   cudaGetDevice(&dev);
   int& mc = max_clusters[dev & 63];
   if (mc == 0) {
     cfg.gridDim = dim3(kNumSMs);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(gateup_pair_kernel), &cfg) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(gateup_pair_kernel<C>), &cfg) !=
+            cudaSuccess ||
         n <= 0) {
       cudaGetLastError();
       n = kNumSMs / 2;
@@ -516,7 +532,7 @@ cudaError_t launch_pair(const GateUpLaunch& L, const void* a, const void* b, cud
     mc = std::min(n, kNumSMs / 2);
   }
   cfg.gridDim = dim3(2 * std::min(p.num_n, mc));
-  return cudaLaunchKernelEx(&cfg, gateup_pair_kernel, p);
+  return cudaLaunchKernelEx(&cfg, gateup_pair_kernel<C>, p);
 }
 
 // ---------------------------------------------------------------------------
@@ -717,7 +733,15 @@ cudaError_t launch_gateup(const GateUpLaunch& L, const void* a, const void* b, c
         if (cand[c] > 0 && (best < 0 || cand[c] < cand[best])) best = c;
     if (best == 0) {
       // SwiGLU with 256-column pair tiles (the same CTA count): the CTA-pair form
-      if (L.mode == 1 && L.M > kBM && L.I % 256 == 0) return launch_pair(L, a, b, stream);
+      if (L.mode == 1 && L.M > kBM) {
+        // of the pair tiles (256 / 224 columns), the one with the least
+        // column work per SM: rounds of resident pairs x tile width
+        const int64_t pairs = sms / 2;
+        const int64_t w256 = L.I % 256 == 0 ? (L.I / 256 + pairs - 1) / pairs * 256 : -1;
+        const int64_t w224 = L.I % 224 == 0 ? (L.I / 224 + pairs - 1) / pairs * 224 : -1;
+        if (w224 > 0 && (w256 < 0 || w224 < w256)) return launch_pair<112>(L, a, b, stream);
+        if (w256 > 0) return launch_pair<128>(L, a, b, stream);
+      }
       return launch_bn<128, 2>(L, a, b, stream);
     }
     if (best == 2) return launch_bn<64, 1>(L, a, b, stream);
