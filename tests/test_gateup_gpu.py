@@ -30,7 +30,7 @@ def _within_one_ulp(d, ref):
     assert (err <= bound).all(), f"max excess {(err - bound).max():.3e} at {np.unravel_index(np.argmax(err - bound), err.shape)}"
 
 
-@pytest.mark.parametrize("M", [1, 16, 37, 128, 130, 256])
+@pytest.mark.parametrize("M", [1, 16, 30, 37, 128, 130, 256])
 def test_swiglu_small_vs_oracle(M):
     import torch
     Hh.need_cuda()

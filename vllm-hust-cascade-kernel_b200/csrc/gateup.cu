@@ -547,7 +547,9 @@ cudaError_t launch_pair(const GateUpLaunch& L, const void* a, const void* b, cud
 // ---------------------------------------------------------------------------
 template <int MP>
 struct SwapCfg {
-  static constexpr int kStages = MP <= 64 ? 3 : 2;
+  // deep enough to keep ~17 MB of weight tiles in flight over the 224 CTAs of
+  // an 8B-sized call, within two CTAs per SM
+  static constexpr int kStages = MP <= 32 ? 5 : (MP <= 64 ? 4 : 2);
   static constexpr int kABytes = 128 * kBK * 2;            // W tile: 16 KB
   static constexpr int kBBytes = MP * kBK * 2;             // X tile
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -558,12 +560,14 @@ struct SwapCfg {
   static constexpr int kBarOff = kXchgOff + kXchgBytes;
   static_assert(kBarOff % 16 == 0, "mbarriers need 8-byte alignment");
   static constexpr int kSmem = kBarOff + 256 + 1024;
+  static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
+  static_assert(kStages <= 5, "SwapBars holds 5 stages");
   static constexpr uint32_t kTmemCols = MP < 32 ? 32 : MP;
 };
 
 struct __align__(8) SwapBars {
-  uint64_t full[3];
-  uint64_t empty[3];
+  uint64_t full[5];
+  uint64_t empty[5];
   uint64_t acc_full;
   uint32_t tmem_base;
 };
