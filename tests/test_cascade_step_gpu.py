@@ -231,11 +231,15 @@ def test_layers_graph_steps_and_host_io():
         CascadeLayersGraph(steps, host_io=ios[:1])
 
 
-def test_layers_graph_overlapped_host_io_reuses_buffers_safely():
-    """overlap_io=True where steps share device input buffers (steps 0 and 2
-    load different host queries into the same dev_in, as do 1 and 3): step 2's
-    host->device copy must wait until step 0 has read the buffer, so every
-    step's pinned output equals the eager step on its OWN query."""
+@pytest.mark.parametrize("use,io_group", [([0, 1, 0, 1], 1), ([0, 1, 0, 1], 4), ([0, 1, 2, 0, 1, 2, 0], 4),
+                                          ([0, 1, 2, 3, 0, 1, 2, 3, 0], 2), ([0, 0, 1], 4)])
+def test_layers_graph_overlapped_host_io_reuses_buffers_safely(use, io_group):
+    """overlap_io=True where steps share device input buffers (e.g. steps 0
+    and 2 load different host queries into the same dev_in): a step's
+    host->device copy must wait until the earlier step on that buffer has
+    read it, and a copy group ends before a buffer repeats, so every step's
+    pinned output equals the eager step on its OWN query -- for copy groups
+    of 1, 2 and 4 steps."""
     import torch
     from cascade_kernel.cascade import CascadeLayersGraph, cascade_decode
     Hh.need_cuda()
@@ -245,10 +249,9 @@ def test_layers_graph_overlapped_host_io_reuses_buffers_safely():
     t = w.tables
     gen = torch.Generator(device="cuda").manual_seed(9)
     k2, v2 = (torch.randn(x.shape, device="cuda", generator=gen).to(x.dtype) for x in (w.k_pool, w.v_pool))
-    pools = [(w.k_pool, w.v_pool), (k2, v2), (k2, v2), (w.k_pool, w.v_pool)]
+    pools = [((w.k_pool, w.v_pool), (k2, v2))[(i * 5 // 3) % 2] for i in range(len(use))]
     nbytes = w.q.numel() * w.q.element_size()
-    dins = [torch.empty(nbytes, dtype=torch.uint8, device="cuda") for _ in range(2)]
-    use = [0, 1, 0, 1]
+    dins = [torch.empty(nbytes, dtype=torch.uint8, device="cuda") for _ in range(max(use) + 1)]
     qs = [torch.randn(w.q.shape, device="cuda", generator=gen).to(w.q.dtype) for _ in use]
     steps, io = [], []
     for i, b in enumerate(use):
@@ -257,7 +260,7 @@ def test_layers_graph_overlapped_host_io_reuses_buffers_safely():
         out_h = torch.empty(w.q.shape, dtype=w.q.dtype).pin_memory()
         steps.append((dins[b].view(w.q.dtype).view(w.q.shape), pools[i][0], pools[i][1], t))
         io.append((hin, dins[b], out_h))
-    g = CascadeLayersGraph(steps, host_io=io, overlap_io=True)
+    g = CascadeLayersGraph(steps, host_io=io, overlap_io=True, io_group=io_group)
     for _ in range(2):
         g.replay()
         torch.cuda.synchronize()

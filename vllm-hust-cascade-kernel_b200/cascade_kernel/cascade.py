@@ -86,14 +86,22 @@ class CascadeLayersGraph:
     step's output is copied into the pinned host tensor ``host_out``.
 
     ``overlap_io=True`` issues those copies on two copy streams inside the
-    graph instead of in line with the kernels: step i's host->device copy
-    waits only for the last earlier step that reads the same ``dev_in`` (so
-    it can run while the steps before it compute), step i's kernels wait for
-    that copy, and step i's device->host copy waits only for step i. Every
-    step still moves its own inputs in and its own output out.
+    graph instead of in line with the kernels, in groups of consecutive
+    steps whose ``dev_in`` buffers differ (1, 2, then up to ``io_group``
+    steps but at most half the number of distinct ``dev_in`` buffers, the
+    last step alone, so filling and draining the copy pipeline costs one
+    step's copies as without grouping): a group's host->device
+    copies wait only for the last earlier steps that
+    read the same ``dev_in`` buffers (so they run while earlier steps
+    compute) and complete behind one event that the group's first kernel
+    waits for; the group's device->host copies wait for its last step. Every
+    step still moves its own inputs in and its own output out. Grouping
+    matters because each wait of the kernel stream on a copy-engine event is
+    an edge into the graph's critical path (measured: ~3 us per step with
+    ``io_group=1`` on the C2 step).
     """
 
-    def __init__(self, steps, out_dtype=None, warmup=2, host_io=None, overlap_io=False):
+    def __init__(self, steps, out_dtype=None, warmup=2, host_io=None, overlap_io=False, io_group=4):
         steps = list(steps)
         if not steps:
             raise ValueError("CascadeLayersGraph needs at least one step")
@@ -102,6 +110,8 @@ class CascadeLayersGraph:
                 raise ValueError("CascadeLayersGraph needs uniform prefix groups (tables.uniform_group > 0)")
         if host_io is not None and len(host_io) != len(steps):
             raise ValueError("host_io needs one (host_in, dev_in, host_out) triple per step")
+        if io_group < 1:
+            raise ValueError("io_group must be >= 1")
         self.steps, self.out_dtype, self.host_io = steps, out_dtype, host_io
         io_streams = (torch.cuda.Stream(), torch.cuda.Stream()) if host_io is not None and overlap_io else None
 
@@ -110,26 +120,52 @@ class CascadeLayersGraph:
             s_in, s_out = io_streams
             s_in.wait_stream(main)
             s_out.wait_stream(main)
-            outs, done, last_use = [], [], {}
-            for i, (q, k_pool, v_pool, tables) in enumerate(steps):
-                host_in, dev_in, host_out = host_io[i]
+            # groups of consecutive steps with distinct dev_in, sized 1, 2,
+            # then io_group, with the last step alone: the first kernel waits
+            # for one step's inputs and one step's output drains after the
+            # last kernel, as with per-step copies
+            # a group's copies overlap the previous group's kernels only if
+            # the two groups use different buffers: at most half of them each
+            n_buf = len({io[1].data_ptr() for io in host_io})
+            limit = max(1, min(io_group, n_buf // 2))
+            groups, cur, seen = [], [], set()
+            for i in range(len(steps)):
+                key = host_io[i][1].data_ptr()
+                cap = min(limit, 1 << len(groups))
+                if len(cur) >= cap or key in seen:
+                    groups.append(cur)
+                    cur, seen = [], set()
+                cur.append(i)
+                seen.add(key)
+            groups.append(cur)
+            if len(groups[-1]) > 1:
+                groups.append([groups[-1].pop()])
+            outs, fin_of, last_use = [None] * len(steps), {}, {}
+            for grp in groups:
                 with torch.cuda.stream(s_in):
-                    j = last_use.get(dev_in.data_ptr())
-                    if j is not None:
-                        s_in.wait_event(done[j])
-                    dev_in.copy_(host_in, non_blocking=True)
+                    waited = set()
+                    for i in grp:
+                        host_in, dev_in, _ = host_io[i]
+                        j = last_use.get(dev_in.data_ptr())
+                        if j is not None and id(fin_of[j]) not in waited:
+                            s_in.wait_event(fin_of[j])
+                            waited.add(id(fin_of[j]))
+                        dev_in.copy_(host_in, non_blocking=True)
                     loaded = torch.cuda.Event()
                     loaded.record(s_in)
                 main.wait_event(loaded)
-                out = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
+                for i in grp:
+                    q, k_pool, v_pool, tables = steps[i]
+                    outs[i] = cascade_decode(q, k_pool, v_pool, tables, out_dtype)
                 fin = torch.cuda.Event()
                 fin.record(main)
-                done.append(fin)
-                last_use[dev_in.data_ptr()] = i
+                for i in grp:
+                    fin_of[i] = fin
+                    last_use[host_io[i][1].data_ptr()] = i
                 with torch.cuda.stream(s_out):
                     s_out.wait_event(fin)
-                    host_out.copy_(out, non_blocking=True)
-                outs.append(out)
+                    for i in grp:
+                        host_io[i][2].copy_(outs[i], non_blocking=True)
             main.wait_stream(s_in)
             main.wait_stream(s_out)
             return outs
