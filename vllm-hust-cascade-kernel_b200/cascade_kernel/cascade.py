@@ -67,6 +67,30 @@ def cascade_decode(q, k_pool, v_pool, tables: CascadeTables, out_dtype=None, fus
     return npu.cascade_lse_merge(o1, o2, l1, l2, code)
 
 
+def copy_groups(buffers, io_group):
+    """Groups of consecutive steps whose host copies share one event in
+    ``CascadeLayersGraph(overlap_io=True)``; ``buffers[i]`` identifies step
+    i's device input buffer. Groups hold distinct buffers, are sized 1, 2,
+    then up to ``io_group`` steps -- but at most half the distinct buffers,
+    so a group's copies can run while the previous group computes -- and the
+    last step is a group of its own: the first kernel waits for one step's
+    inputs and one step's output drains after the last kernel, as with
+    per-step copies."""
+    limit = max(1, min(io_group, len(set(buffers)) // 2))
+    groups, cur, seen = [], [], set()
+    for i, key in enumerate(buffers):
+        if len(cur) >= min(limit, 1 << len(groups)) or key in seen:
+            groups.append(cur)
+            cur, seen = [], set()
+        cur.append(i)
+        seen.add(key)
+    if cur:
+        groups.append(cur)
+    if groups and len(groups[-1]) > 1:
+        groups.append([groups[-1].pop()])
+    return groups
+
+
 class CascadeLayersGraph:
     """Several cascade decode steps captured back to back in ONE CUDA graph,
     as a decode forward runs attention layer after layer: step i reads its
@@ -120,26 +144,7 @@ class CascadeLayersGraph:
             s_in, s_out = io_streams
             s_in.wait_stream(main)
             s_out.wait_stream(main)
-            # groups of consecutive steps with distinct dev_in, sized 1, 2,
-            # then io_group, with the last step alone: the first kernel waits
-            # for one step's inputs and one step's output drains after the
-            # last kernel, as with per-step copies
-            # a group's copies overlap the previous group's kernels only if
-            # the two groups use different buffers: at most half of them each
-            n_buf = len({io[1].data_ptr() for io in host_io})
-            limit = max(1, min(io_group, n_buf // 2))
-            groups, cur, seen = [], [], set()
-            for i in range(len(steps)):
-                key = host_io[i][1].data_ptr()
-                cap = min(limit, 1 << len(groups))
-                if len(cur) >= cap or key in seen:
-                    groups.append(cur)
-                    cur, seen = [], set()
-                cur.append(i)
-                seen.add(key)
-            groups.append(cur)
-            if len(groups[-1]) > 1:
-                groups.append([groups[-1].pop()])
+            groups = copy_groups([io[1].data_ptr() for io in host_io], io_group)
             outs, fin_of, last_use = [None] * len(steps), {}, {}
             for grp in groups:
                 with torch.cuda.stream(s_in):
