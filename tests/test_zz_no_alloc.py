@@ -5,9 +5,17 @@ attention step (a host binding the C ABI without a device allocator, or a
 serving loop whose memory is fixed up front); it keeps its split-KV partials in
 a fixed 16 MiB scratch array inside the library. These checks call it through
 the C ABI and compare it with the allocating entry point, cascade_suffix_decode,
-on two different calls in a row (the second call reuses the scratch the first
-one left behind), and check that oversized or per-request-q-length calls are
-refused before anything runs. This file is collected last on purpose.
+on several different calls in a row (each reuses the scratch the one before
+left behind), cover both the per-item decode and the planned decode (whose
+scratch also holds the device-built item list and its counters), and check
+that oversized or per-request-q-length calls are refused before anything runs.
+
+Ordering: pytest collects test files in name order, and this file's name puts
+it last, so a run that stops at the first failure (``-x``) has already run every
+other test when a failure here stops it. Nothing here depends on that order:
+the first call on a device looks up the scratch array's address whether or not
+other tests ran before, and the file passes alone in a fresh process as well
+as after the rest of the suite.
 """
 import numpy as np
 import pytest
@@ -18,10 +26,12 @@ from oracle import cascade_oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def _case(seed, B, kv_max, H=32, KVH=8, bs=128):
+def _case(seed, B, kv_max, H=32, KVH=8, bs=128, kv_typ=None):
+    """Seeded suffix-decode inputs: kv lengths U[0, kv_typ or kv_max], the
+    first request at kv_max (so the block table spans kv_max tokens)."""
     import torch
     rng = np.random.default_rng(seed)
-    kv = rng.integers(0, kv_max + 1, size=B)
+    kv = rng.integers(0, (kv_typ or kv_max) + 1, size=B)
     kv[0] = kv_max                      # at least one request uses every split
     pages = [(int(k) + bs - 1) // bs for k in kv]
     n = sum(pages) + 1
@@ -55,11 +65,17 @@ def _noalloc(args):
 def test_noalloc_matches_allocating_entry_on_two_calls():
     Hh.need_cuda()
     C = Hh.capi()
-    # two different problems, both split into several KV partials
-    cases = [_case(11, B=64, kv_max=1024), _case(12, B=40, kv_max=768, H=40)]
+    # three different problems, all split into several KV partials: two take
+    # the per-item decode, the third (256 requests x 8 kv heads over a
+    # 4608-token block table) the planned decode, whose scratch also holds
+    # the item list, its count and the per-kv-head counters
+    cases = [_case(11, B=64, kv_max=1024), _case(12, B=40, kv_max=768, H=40),
+             _case(13, B=256, kv_max=4608, H=8, KVH=8, kv_typ=600)]
+    kernels = []
     for args in cases:
         desc = C.paged_desc(*args, 1)
         assert C.suffix_workspace_size(desc) > 0       # the scratch is really used
+        kernels.append(C.plan(desc, 1, True).kernel)
         ref_out, ref_lse = Hh.run_capi_paged(*args, 1, suffix=True)
         out, lse = _noalloc(args)
         o, r = Hh.dev_to_f64(out), Hh.dev_to_f64(ref_out)
@@ -70,6 +86,7 @@ def test_noalloc_matches_allocating_entry_on_two_calls():
         fin = np.isfinite(lr)
         assert np.array_equal(np.isneginf(l), np.isneginf(lr))
         assert np.abs(l[fin] - lr[fin]).max() <= 1e-5
+    assert kernels == [0, 0, 2]
 
 
 def test_noalloc_refuses_oversized_and_legacy_calls():

@@ -13,7 +13,9 @@
 // In host code `g_noalloc_scratch` names a host-side stand-in, not device
 // memory, so its device address is resolved with cudaGetSymbolAddress on
 // each device (with that device current) the first time the entry point runs
-// there, and that address is what the kernels receive.
+// there, and that address is what the kernels receive. Only a successful
+// lookup is remembered: a failed one is reported to that caller and tried
+// again on the next call.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -29,9 +31,25 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
-std::once_flag g_setup_once[kMaxDevices];
-void* g_scratch_addr[kMaxDevices];
-cudaError_t g_setup_err[kMaxDevices];
+std::mutex g_setup_mu;
+void* g_scratch_addr[kMaxDevices];  // null until the lookup succeeded on that device
+
+// Device address of the scratch array on the current device `dev`, or null
+// with *err set when the lookup fails.
+void* scratch_address(int dev, cudaError_t* err) {
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  *err = cudaSuccess;
+  if (g_scratch_addr[dev] != nullptr) return g_scratch_addr[dev];
+  void* ptr = nullptr;
+  *err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (*err != cudaSuccess || ptr == nullptr) {
+    if (*err == cudaSuccess) *err = cudaErrorInvalidSymbol;
+    cudaGetLastError();  // the failure is returned to this caller, not left for the next CUDA call
+    return nullptr;
+  }
+  g_scratch_addr[dev] = ptr;
+  return ptr;
+}
 
 }  // namespace
 
@@ -45,14 +63,10 @@ extern "C" int cascade_suffix_decode_noalloc(const cascade_paged_attn_t* p, void
     snprintf(msg, sizeof(msg), "%s: no usable current CUDA device", op);
     return cascade::set_error(CASCADE_ERR_CUDA, msg);
   }
-  std::call_once(g_setup_once[dev], [dev] {
-    void* ptr = nullptr;
-    g_setup_err[dev] = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    g_scratch_addr[dev] = ptr;
-  });
-  if (g_setup_err[dev] != cudaSuccess || g_scratch_addr[dev] == nullptr) {
+  void* scratch = scratch_address(dev, &e);
+  if (scratch == nullptr) {
     snprintf(msg, sizeof(msg), "%s: cudaGetSymbolAddress of the scratch array failed (%s)", op,
-             cudaGetErrorString(g_setup_err[dev]));
+             cudaGetErrorString(e));
     return cascade::set_error(CASCADE_ERR_CUDA, msg);
   }
   if (p == nullptr) return cascade::set_error(CASCADE_ERR_INVALID, "cascade_suffix_decode_noalloc: null argument");
@@ -69,5 +83,5 @@ extern "C" int cascade_suffix_decode_noalloc(const cascade_paged_attn_t* p, void
              op, need, kScratchBytes);
     return cascade::set_error(CASCADE_ERR_UNSUPPORTED, msg);
   }
-  return cascade_suffix_decode(p, out, lse, need ? g_scratch_addr[dev] : nullptr, need ? kScratchBytes : 0, stream);
+  return cascade_suffix_decode(p, out, lse, need ? scratch : nullptr, need ? kScratchBytes : 0, stream);
 }
