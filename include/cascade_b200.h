@@ -71,13 +71,43 @@ typedef struct cascade_paged_attn {
   int64_t block_cols;
   int64_t q_seqlen_value;
   int32_t dtype; /* cascade_dtype of query/key/value: BF16 or FP16 */
-  int32_t flags; /* reserved, pass 0 */
+  int32_t flags; /* CASCADE_FLAG_* bits, normally 0 */
 } cascade_paged_attn_t;
 
 /* cascade_paged_attn_t.flags bit: write the split-KV partials
  * (workspace layout below) and skip the final combine; out/lse are not
  * touched. Used to time or chain the attention kernel alone. */
 #define CASCADE_FLAG_PARTIALS_ONLY 1
+
+/* cascade_paged_attn_t.flags bit, a test hook for the kernels' bounded waits
+ * (no counterpart in the reference): the attention kernel's consumer warps
+ * first wait on a barrier that nothing completes, with a 1 ms limit instead
+ * of the default 100 ms. The wait runs out, the CTA aborts (its other waits
+ * return at once, producers stop and drain their copies in flight, TMEM is
+ * freed) and the call ends with bit 1 of cascade_device_error() set. The
+ * outputs of such a call are garbage. */
+#define CASCADE_FLAG_DEBUG_STALL 2
+
+/* cascade_paged_attn_t.flags bit, a debug mode: before launching, read the
+ * block table and the kv lengths back to the host (a synchronising copy) and
+ * reject the call with CASCADE_ERR_INVALID if a page a request reads has a
+ * block id outside [0, num_blocks) (cascade_check_block_table below). Without
+ * it the kernels still never read outside the pool: such a page reads as
+ * zeros and bit 2 of cascade_device_error() is set. */
+#define CASCADE_FLAG_CHECK_BLOCK_IDS 4
+
+/* Host-side check of a block table against the paging contract (no CUDA
+ * calls; host memory): every page a request reads -- entries
+ * [0, ceil(kv_lens[r] / block_size)) of row r -- must hold a block id in
+ * [0, num_blocks), and ceil(kv_lens[r] / block_size) must not exceed cols.
+ * bt: int32 [rows, cols] (row stride cols); kv_lens: int64 [rows].
+ * Returns 0, or CASCADE_ERR_INVALID with the first offending (row, column)
+ * in *bad_row / *bad_col (either may be NULL) and a message naming them. The
+ * reference guards the same contract statically
+ * (ascend-kernel/csrc/ops/fa_fp32_stage1/op_kernel/kernel_fa_fp32_stage1.cpp:107-112). */
+CASCADE_API int cascade_check_block_table(const int32_t *bt, int64_t rows, int64_t cols, const int64_t *kv_lens,
+                                          int64_t block_size, int64_t num_blocks, int64_t *bad_row,
+                                          int64_t *bad_col);
 
 /* Bytes of device workspace a call with this description needs (split-KV
  * partials). Depends on shapes only, never on the seqlen values. 0 = none. */

@@ -28,6 +28,7 @@ EXPORTED = [
     "cascade_device_error",
     "cascade_version",
     "cascade_plan_paged_attn",
+    "cascade_check_block_table",
 ]
 
 
@@ -103,6 +104,8 @@ def load():
     lib.cascade_version.restype = ctypes.c_int
     lib.cascade_plan_paged_attn.argtypes = [P, i64, i32, ctypes.POINTER(AttnPlan)]
     lib.cascade_plan_paged_attn.restype = ctypes.c_int
+    lib.cascade_check_block_table.argtypes = [vp, i64, i64, vp, i64, i64, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+    lib.cascade_check_block_table.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -139,6 +142,8 @@ def dtype_code(torch_dtype):
 
 
 FLAG_PARTIALS_ONLY = 1
+FLAG_DEBUG_STALL = 2      # test hook: the kernel's bounded waits run out (1 ms) and the call aborts
+FLAG_CHECK_BLOCK_IDS = 4  # debug mode: read the block table back and check it before launching
 
 
 def paged_desc(query, key, value, block_table, q_seqlens, kv_seqlens, q_seqlen_value=0, *,
@@ -168,6 +173,24 @@ def plan(desc, max_q, suffix=False):
     p = AttnPlan()
     check(load().cascade_plan_paged_attn(ctypes.byref(desc), max_q, int(suffix), ctypes.byref(p)))
     return p
+
+
+def check_block_table(bt, kv_lens, block_size, num_blocks):
+    """Host-side paging-contract check (cascade_check_block_table) of numpy
+    arrays: bt int32 [rows, cols], kv_lens int64 [rows]. Returns None, or
+    raises CascadeError whose ``bad`` attribute is the first offending
+    (row, column)."""
+    import numpy as np
+    bt = np.ascontiguousarray(bt, dtype=np.int32)
+    kv = np.ascontiguousarray(kv_lens, dtype=np.int64)
+    rows, cols = bt.shape
+    r, c = ctypes.c_int64(-1), ctypes.c_int64(-1)
+    rc = load().cascade_check_block_table(bt.ctypes.data, rows, cols, kv.ctypes.data, int(block_size),
+                                          int(num_blocks), ctypes.byref(r), ctypes.byref(c))
+    if rc != OK:
+        err = CascadeError(rc, load().cascade_last_error().decode())
+        err.bad = (r.value, c.value)
+        raise err
 
 
 def stream_ptr(stream=None):

@@ -183,6 +183,48 @@ int read_and_check_seqlens(const cascade_paged_attn_t* p, const char* op, bool a
   return CASCADE_OK;
 }
 
+int check_table(const char* op, const int32_t* bt, int64_t rows, int64_t cols, const int64_t* kv_lens,
+                int64_t block_size, int64_t num_blocks, int64_t* bad_row, int64_t* bad_col) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const int64_t kv = kv_lens[r] < 0 ? 0 : kv_lens[r];
+    const int64_t pages = ceil_div(kv, block_size);
+    if (pages > cols) {
+      if (bad_row) *bad_row = r;
+      if (bad_col) *bad_col = cols;
+      return fail(CASCADE_ERR_INVALID, "%s: block_table row %lld needs %lld pages for kv %lld but has %lld columns",
+                  op, static_cast<long long>(r), static_cast<long long>(pages), static_cast<long long>(kv),
+                  static_cast<long long>(cols));
+    }
+    for (int64_t c = 0; c < pages; ++c) {
+      const int32_t id = bt[r * cols + c];
+      if (id < 0 || id >= num_blocks) {
+        if (bad_row) *bad_row = r;
+        if (bad_col) *bad_col = c;
+        return fail(CASCADE_ERR_INVALID, "%s: block_table[%lld][%lld] = %d is outside [0, num_blocks=%lld)", op,
+                    static_cast<long long>(r), static_cast<long long>(c), static_cast<int>(id),
+                    static_cast<long long>(num_blocks));
+      }
+    }
+  }
+  return CASCADE_OK;
+}
+
+// Debug mode (CASCADE_FLAG_CHECK_BLOCK_IDS): read the block table and the kv
+// lengths back and check every page the call will read.
+int read_and_check_table(const cascade_paged_attn_t* p, const char* op, cudaStream_t stream) {
+  std::vector<int32_t> bt(static_cast<size_t>(p->batch * p->block_cols));
+  std::vector<int64_t> kv(static_cast<size_t>(p->batch));
+  cudaError_t e = cudaSuccess;
+  if (!bt.empty())
+    e = cudaMemcpyAsync(bt.data(), p->block_table, bt.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(kv.data(), p->actual_kv_seqlens, kv.size() * sizeof(int64_t), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(op, e);
+  return check_table(op, bt.data(), p->batch, p->block_cols, kv.data(), p->block_size, p->num_blocks, nullptr,
+                     nullptr);
+}
+
 // Validation, seqlen read-back (legacy path), planning and tensor maps of one
 // paged-attention call. On success *L holds everything but the output and
 // workspace pointers. Returns CASCADE_OK with plan->num_splits == 0 for an
@@ -200,6 +242,10 @@ int prepare_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, cu
   int64_t max_q = p->q_seqlen_value;
   if (p->q_seqlen_value == 0) {
     rc = read_and_check_seqlens(p, op, suffix, stream, &max_q);
+    if (rc) return rc;
+  }
+  if (p->flags & CASCADE_FLAG_CHECK_BLOCK_IDS) {
+    rc = read_and_check_table(p, op, stream);
     if (rc) return rc;
   }
   rc = cascade_plan_paged_attn(p, max_q, suffix ? 1 : 0, plan);
@@ -233,6 +279,8 @@ int prepare_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, cu
   L->out_dtype = suffix ? p->dtype : CASCADE_FP32;
   L->lse_stride = suffix ? 1 : 8;
   L->partial_out = (p->flags & CASCADE_FLAG_PARTIALS_ONLY) ? 1 : 0;
+  L->debug_stall = (p->flags & CASCADE_FLAG_DEBUG_STALL) ? 1 : 0;
+  L->wait_limit_us = L->debug_stall ? 1000u : 0u;
   L->scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(kHeadDim)) * 1.4426950408889634);
   return CASCADE_OK;
 }
@@ -334,6 +382,15 @@ int cascade_device_error(uint32_t* word) {
   if (e != cudaSuccess) return cuda_fail("cascade_device_error", e);
   if (word) *word = v;
   return CASCADE_OK;
+}
+
+int cascade_check_block_table(const int32_t* bt, int64_t rows, int64_t cols, const int64_t* kv_lens,
+                              int64_t block_size, int64_t num_blocks, int64_t* bad_row, int64_t* bad_col) {
+  const char* op = "cascade_check_block_table";
+  if (rows < 0 || cols < 0 || block_size <= 0 || num_blocks < 0)
+    return fail(CASCADE_ERR_INVALID, "%s: negative size", op);
+  if (rows > 0 && (!kv_lens || (cols > 0 && !bt))) return fail(CASCADE_ERR_INVALID, "%s: null pointer", op);
+  return check_table(op, bt, rows, cols, kv_lens, block_size, num_blocks, bad_row, bad_col);
 }
 
 int cascade_plan_paged_attn(const cascade_paged_attn_t* p, int64_t max_q_seqlen, int32_t suffix_mode,

@@ -64,8 +64,16 @@ struct __align__(8) GemmBars {
   uint64_t empty[kStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
+  uint64_t drain;           // an aborting MMA issuer's last commit
   uint32_t tmem_base;
 };
+
+// Teardown of an aborting CTA's producer: wait (bounded) for the TMA loads of
+// the last NS ring positions it issued, [0, issued), one per stage.
+template <int NS>
+__device__ __forceinline__ void drain_loads(uint64_t* full, int issued) {
+  for (int it = issued > NS ? issued - NS : 0; it < issued; ++it) mbar_wait_drain(&full[it % NS], (it / NS) & 1);
+}
 
 struct GemmParams {
   CUtensorMap tm_a;   // X [M, K], box {64, 128}
@@ -103,7 +111,9 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
       mbar_init(&bars->acc_full[a], 1);
       mbar_init(&bars->acc_empty[a], 4 * 32);
     }
+    mbar_init(&bars->drain, 1);
     fence_mbar_init();
+    cta_wait_init();
   }
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, C::kTmemCols);
@@ -119,12 +129,13 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
       tma_prefetch_desc(&p.tm_a);
       tma_prefetch_desc(&p.tm_b);
       int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int tile = blockIdx.x; tile < num_tiles && !cta_aborted(); tile += gridDim.x) {
         const int m0 = (tile % p.num_m) * (MT * kBM);
         const int n0 = (tile / p.num_m) * BN;
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int st = it % NS;
           if (it >= NS) mbar_wait(&bars->empty[st], ((it / NS) - 1) & 1);
+          if (cta_aborted()) break;
           uint8_t* sa = smem + C::kStageOff + st * C::kStageBytes;
           uint8_t* sb = sa + C::kABytes;
           mbar_arrive_expect_tx(&bars->full[st], C::kStageBytes);
@@ -134,13 +145,14 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
           tma_load_2d(sb + BN * 128, &p.tm_b, &bars->full[st], kb * kBK, p.I + n0);
         }
       }
+      if (cta_aborted()) drain_loads<NS>(bars->full, it);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(128, 2 * BN, 1, 0, 0);
       const uint32_t sbase = smem_u32(smem + C::kStageOff);
       int it = 0, tc = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tc) {
+      for (int tile = blockIdx.x; tile < num_tiles && !cta_aborted(); tile += gridDim.x, ++tc) {
         const int ab = tc % NA;
         if (tc >= NA) mbar_wait(&bars->acc_empty[ab], ((tc / NA) - 1) & 1);
         tc_fence_after();
@@ -148,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int st = it % NS;
           mbar_wait(&bars->full[st], (it / NS) & 1);
+          if (cta_aborted()) break;
           tc_fence_after();
           const uint32_t a0 = sbase + st * C::kStageBytes;
           const uint32_t b0 = a0 + C::kABytes;
@@ -162,6 +175,10 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_kernel(const __grid_consta
           umma_commit(&bars->empty[st]);
         }
         umma_commit(&bars->acc_full[ab]);
+      }
+      if (cta_aborted()) {
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
       }
     }
   } else {
@@ -343,6 +360,7 @@ struct __align__(8) PairBars {
   uint64_t empty[kPairStages];  // each CTA's: the pair's MMAs read the stage
   uint64_t acc_full;            // each CTA's: the tile's MMAs are done
   uint64_t acc_empty;           // rank 0's: both CTAs' epilogues read TMEM
+  uint64_t drain;               // rank 0's: an aborting MMA issuer's last commit
   uint32_t tmem_base;
 };
 
@@ -364,7 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
     }
     mbar_init(&bars->acc_full, 1);
     mbar_init(&bars->acc_empty, 2);
+    mbar_init(&bars->drain, 1);
     fence_mbar_init();
+    cta_wait_init();
   }
   if (warp == 1) {
     tmem_alloc_pair(&bars->tmem_base, 512);
@@ -381,11 +401,12 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
       tma_prefetch_desc(&p.tm_a);
       tma_prefetch_desc(&p.tm_b);
       int it = 0;
-      for (int tile = cluster; tile < num_tiles; tile += nclusters) {
+      for (int tile = cluster; tile < num_tiles && !cta_aborted(); tile += nclusters) {
         const int wrow = (rank == 0 ? 0 : p.I) + tile * 2 * C;  // gate rows (rank 0) or up rows (rank 1)
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int st = it % kPairStages;
           if (it >= kPairStages) mbar_wait_cluster(&bars->empty[st], ((it / kPairStages) - 1) & 1);
+          if (cta_aborted()) break;
           const uint32_t full_l = mapa_shared(smem_u32(&bars->full[st]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&bars->full[st], 2 * Cfg::kStageBytes);
           uint8_t* sa = smem + st * Cfg::kStageBytes;
@@ -395,17 +416,31 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
           tma_load_2d_pair(sb + Cfg::kBHalf, &p.tm_b, full_l, kb * kBK, wrow + C);
         }
       }
+      if (cta_aborted()) {
+        if (rank == 0) {
+          // both CTAs' loads of a stage complete on rank 0's barrier
+          for (int i = it > kPairStages ? it - kPairStages : 0; i < it; ++i)
+            mbar_wait_cluster_drain(&bars->full[i % kPairStages], (i / kPairStages) & 1);
+        } else {
+          // rank 1 cannot observe rank 0's barriers: give its own last loads
+          // time to land (a TMA copy takes microseconds) before teardown
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000) {
+          }
+        }
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       const uint32_t idesc = make_idesc_f16(256, 2 * C, 1, 0, 0);
       int it = 0, tc = 0;
-      for (int tile = cluster; tile < num_tiles; tile += nclusters, ++tc) {
+      for (int tile = cluster; tile < num_tiles && !cta_aborted(); tile += nclusters, ++tc) {
         if (tc > 0) mbar_wait_cluster(&bars->acc_empty, (tc - 1) & 1);
         tc_fence_after();
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int st = it % kPairStages;
           mbar_wait_cluster(&bars->full[st], (it / kPairStages) & 1);
+          if (cta_aborted()) break;
           tc_fence_after();
           const uint32_t a0 = smem_u32(smem + st * Cfg::kStageBytes);
           const uint32_t b0 = a0 + Cfg::kABytes;
@@ -419,6 +454,10 @@ __global__ void __launch_bounds__(kThreads, 1) gateup_pair_kernel(const __grid_c
           umma_commit_pair(&bars->empty[st], 3);
         }
         umma_commit_pair(&bars->acc_full, 3);
+      }
+      if (cta_aborted()) {
+        umma_commit_pair(&bars->drain, 1);
+        mbar_wait_cluster_drain(&bars->drain, 0);
       }
     }
   } else {
@@ -569,6 +608,7 @@ struct __align__(8) SwapBars {
   uint64_t full[5];
   uint64_t empty[5];
   uint64_t acc_full;
+  uint64_t drain;
   uint32_t tmem_base;
 };
 
@@ -587,7 +627,9 @@ __global__ void __launch_bounds__(kThreads, 2) gateup_swap_kernel(const __grid_c
       mbar_init(&bars->empty[s], 1);
     }
     mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->drain, 1);
     fence_mbar_init();
+    cta_wait_init();
   }
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, C::kTmemCols);
@@ -603,9 +645,11 @@ __global__ void __launch_bounds__(kThreads, 2) gateup_swap_kernel(const __grid_c
       tma_prefetch_desc(&p.tm_a);
       tma_prefetch_desc(&p.tm_b);
       const uint64_t pol = policy_evict_first();  // weights are streamed once
-      for (int kb = 0; kb < p.num_kb; ++kb) {
+      int kb = 0;
+      for (; kb < p.num_kb; ++kb) {
         const int st = kb % C::kStages;
         if (kb >= C::kStages) mbar_wait(&bars->empty[st], ((kb / C::kStages) - 1) & 1);
+        if (cta_aborted()) break;
         uint8_t* sa = smem + st * C::kStageBytes;
         uint8_t* sb = sa + C::kABytes;
         mbar_arrive_expect_tx(&bars->full[st], C::kStageBytes);
@@ -613,6 +657,7 @@ __global__ void __launch_bounds__(kThreads, 2) gateup_swap_kernel(const __grid_c
         tma_load_2d_hint(sa + 64 * 128, &p.tm_b, &bars->full[st], kb * kBK, p.I + n0, pol);  // up rows
         tma_load_2d(sb, &p.tm_a, &bars->full[st], kb * kBK, 0);                           // X rows
       }
+      if (cta_aborted()) drain_loads<C::kStages>(bars->full, kb);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -621,6 +666,7 @@ __global__ void __launch_bounds__(kThreads, 2) gateup_swap_kernel(const __grid_c
       for (int kb = 0; kb < p.num_kb; ++kb) {
         const int st = kb % C::kStages;
         mbar_wait(&bars->full[st], (kb / C::kStages) & 1);
+        if (cta_aborted()) break;
         tc_fence_after();
         const uint32_t a0 = sbase + st * C::kStageBytes;
         const uint32_t b0 = a0 + C::kABytes;
@@ -632,6 +678,10 @@ __global__ void __launch_bounds__(kThreads, 2) gateup_swap_kernel(const __grid_c
         umma_commit(&bars->empty[st]);
       }
       umma_commit(&bars->acc_full);
+      if (cta_aborted()) {
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
+      }
     }
   } else {
     // epilogue warps 2-5: TMEM lane quarter q = warp & 3 (2,3 -> up rows; 0,1 -> gate rows)

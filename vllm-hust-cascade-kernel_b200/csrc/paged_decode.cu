@@ -46,6 +46,7 @@ constexpr int kBtCache = 48;  // block-table entries of one split kept in smem
 struct __align__(8) DecodeBarriers {
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  uint64_t stall;  // never completed: the debug_stall test hook waits on it
   int32_t bt[kBtCache];
 };
 
@@ -71,20 +72,32 @@ __device__ __forceinline__ void store_out(void* out, int out_dtype, size_t idx, 
   }
 }
 
-__device__ __forceinline__ void init_decode_barriers(DecodeBarriers* bars) {
+__device__ __forceinline__ void init_decode_barriers(const PagedAttnLaunch& p, DecodeBarriers* bars) {
   for (int s = 0; s < kStages; ++s) {
     mbar_init(&bars->full[s], 1);
     mbar_init(&bars->empty[s], kConsumerWarps);
   }
+  mbar_init(&bars->stall, 1);
   fence_mbar_init();
+  cta_wait_init(static_cast<uint64_t>(p.wait_limit_us) * 1000);
+}
+
+// Teardown of an aborting CTA (lane 0 of the producer warp): wait, bounded,
+// for the TMA loads of ring positions [begin, end) that may still be in
+// flight -- the last NS of them, one per stage -- so no copy lands in shared
+// memory after the CTA has exited.
+template <int NS>
+__device__ __forceinline__ void drain_ring(uint64_t* full, uint32_t begin, uint32_t end) {
+  for (uint32_t gi = (end - begin > NS ? end - NS : begin); gi < end; ++gi) mbar_wait_drain(&full[gi % NS], (gi / NS) & 1);
 }
 
 // Producer warp of one item: pulls the split's block-table entries
 // (bt_pre0/1 = entries lane and lane + 32, loaded earlier by this warp) into
 // shared memory, then lane 0 streams the item's tiles into the NS-stage ring
-// at ring positions it0, it0 + 1, ...
+// at ring positions it0, it0 + 1, ... Returns (in lane 0) the number of tiles
+// issued: fewer than ntiles only when the CTA is aborting.
 template <int NS, bool kBtFilled = false>
-__device__ __forceinline__ void produce_tiles(const PagedAttnLaunch& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+__device__ __forceinline__ int produce_tiles(const PagedAttnLaunch& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                               int32_t* bt_smem, int b, int g, int s_begin, int s_end, int kv,
                                               int ntiles, uint32_t it0, int bt_pre0, int bt_pre1) {
   const int lane = threadIdx.x & 31;
@@ -103,16 +116,18 @@ __device__ __forceinline__ void produce_tiles(const PagedAttnLaunch& p, uint8_t*
     if (lane + 32 < nbt) bt_smem[lane + 32] = bt_pre1;
   }
   __syncwarp();
+  int issued = 0;
   if (lane == 0) {
     tma_prefetch_desc(&p.tmap_k);
     tma_prefetch_desc(&p.tmap_v);
     const int box_rows = bs < kTile ? bs : kTile;
     const int oob_row = p.num_blocks * bs;  // fully out of range -> zero fill
     const uint64_t pol = policy_evict_first();
-    for (int i = 0; i < ntiles; ++i) {
+    for (int i = 0; i < ntiles; ++i, ++issued) {
       const uint32_t gi = it0 + i;  // ring position of this tile in the CTA's lifetime
       const int st = gi % NS;
       if (gi >= NS) mbar_wait(&empty[st], ((gi / NS) - 1) & 1);
+      if (cta_aborted()) break;
       uint8_t* sk = smem + st * kStageBytes;
       uint8_t* sv = sk + kKBytes;
       mbar_arrive_expect_tx(&full[st], kStageBytes);
@@ -121,7 +136,7 @@ __device__ __forceinline__ void produce_tiles(const PagedAttnLaunch& p, uint8_t*
         const int t = t_tile + off;
         const int page = t / bs;
         int row = oob_row;
-        if (page < npages) row = (cached ? bt_smem[page - first_page] : bt[page]) * bs + (t % bs);
+        if (page < npages) row = paged_row(cached ? bt_smem[page - first_page] : bt[page], t, bs, p.num_blocks, oob_row);
         const int x0 = g * kHeadDim;
         uint8_t* dk = sk + off * 128;
         uint8_t* dv = sv + off * 128;
@@ -132,6 +147,7 @@ __device__ __forceinline__ void produce_tiles(const PagedAttnLaunch& p, uint8_t*
       }
     }
   }
+  return issued;
 }
 
 // Q A-fragments of this thread (rows gq and gq+8, 8 k-steps over the 128
@@ -180,7 +196,7 @@ __device__ __forceinline__ void load_q_frags(const PagedAttnLaunch& p, const uin
 // maxima (log2 units) and quad-reduced row sums.
 template <bool kFp16, int NS>
 __device__ __forceinline__ void consume_tiles(const PagedAttnLaunch& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
-                                              uint32_t it0, int ntiles, int s_begin, int s_end,
+                                              uint64_t* stall, uint32_t it0, int ntiles, int s_begin, int s_end,
                                               const uint32_t (&qa)[8][4], float (&o)[16][4], float& m0, float& m1,
                                               float& l0, float& l1) {
   const int warp = threadIdx.x >> 5;
@@ -194,6 +210,7 @@ __device__ __forceinline__ void consume_tiles(const PagedAttnLaunch& p, uint8_t*
   l0 = 0.f;        // this thread's share of the row sums
   l1 = 0.f;
 
+  if (p.debug_stall) mbar_wait(stall, 0);  // test hook: runs into the wait limit, the CTA aborts
   const uint32_t smem_base = smem_u32(smem);
   const int wrow = warp * 16;  // this warp's first token row within a tile
   // ldmatrix row addresses (matrix index = lane / 8, row = lane % 8)
@@ -433,13 +450,14 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
   }
 
   if (init_bars) {
-    if (threadIdx.x == 0) init_decode_barriers(bars);
+    if (threadIdx.x == 0) init_decode_barriers(p, bars);
     __syncthreads();
   }
 
   if (warp == kConsumerWarps) {
-    produce_tiles<kStages>(p, smem, bars->full, bars->empty, bars->bt, b, g, s_begin, s_end, kv, ntiles, it0, bt_pre0,
-                           bt_pre1);
+    const int issued = produce_tiles<kStages>(p, smem, bars->full, bars->empty, bars->bt, b, g, s_begin, s_end, kv,
+                                              ntiles, it0, bt_pre0, bt_pre1);
+    if (lane == 0 && cta_aborted()) drain_ring<kStages>(bars->full, it0, it0 + issued);
     return ntiles;
   }
 
@@ -447,7 +465,8 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
   load_q_frags(p, nullptr, nrows, tok0, g, qa);
   float o[16][4];
   float m0, m1, l0, l1;
-  consume_tiles<kFp16, kStages>(p, smem, bars->full, bars->empty, it0, ntiles, s_begin, s_end, qa, o, m0, m1, l0, l1);
+  consume_tiles<kFp16, kStages>(p, smem, bars->full, bars->empty, &bars->stall, it0, ntiles, s_begin, s_end, qa, o, m0,
+                                m1, l0, l1);
   // All tiles are consumed (every full barrier was waited by every warp), so
   // the stage ring is free for the merge once all consumer warps reach its
   // first barrier.
@@ -497,6 +516,9 @@ struct __align__(16) StreamBarriers {
   uint64_t empty[kSStages];
   uint64_t item_full[2];   // slot written (32 fetcher lanes)
   uint64_t item_empty[2];  // slot consumed (producer + one arrive per consumer warp)
+  uint64_t stall;          // never completed: the debug_stall test hook waits on it
+  int32_t code_bcast;      // the consumers' item code, read once and shared (named barrier 1)
+  int32_t pad[3];
   StreamSlot slot[2];
 };
 
@@ -522,7 +544,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       mbar_init(&bars->item_full[q], 32);
       mbar_init(&bars->item_empty[q], 1 + kConsumerWarps);
     }
+    mbar_init(&bars->stall, 1);
     fence_mbar_init();
+    cta_wait_init(static_cast<uint64_t>(p.wait_limit_us) * 1000);
   }
   pdl_wait();  // the item list, its count and the zeroed counters are complete
   __syncthreads();
@@ -547,8 +571,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       const int q = j & 1;
       StreamSlot& sl = bars->slot[q];
       if (j >= 2) mbar_wait(&bars->item_empty[q], ((j >> 1) - 1) & 1);
+      // an aborting CTA takes no more items: it writes the end code at once
       int item = 0;
-      if (lane == 0) item = atomicAdd(p.plan_counters + g, 1);
+      if (lane == 0) item = cta_aborted() ? count : atomicAdd(p.plan_counters + g, 1);
       item = __shfl_sync(0xffffffffu, item, 0);
       const int code = item < count ? p.plan_items[item] : -1;
       if (code >= 0) {
@@ -579,26 +604,37 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       const int q = j & 1;
       StreamSlot& sl = bars->slot[q];
       mbar_wait(&bars->item_full[q], (j >> 1) & 1);
-      const int code = sl.code;
+      // one lane decides for the warp (an aborting CTA's slots are not
+      // protected by their barriers any more)
+      int code = 0;
+      if (lane == 0) code = cta_aborted() ? -1 : sl.code;
+      code = __shfl_sync(0xffffffffu, code, 0);
       if (code < 0) break;
       const int split = code & 0xFF, b = code >> 8;
       const int s_begin = split * p.split_tokens;
       const int kv = sl.kv;
       const int s_end = min(kv, s_begin + p.split_tokens);
       const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
-      produce_tiles<kSStages, true>(p, smem, bars->full, bars->empty, sl.bt, b, g, s_begin, s_end, kv, ntiles, it0, 0,
-                                    0);
+      int issued = produce_tiles<kSStages, true>(p, smem, bars->full, bars->empty, sl.bt, b, g, s_begin, s_end, kv,
+                                                 ntiles, it0, 0, 0);
+      issued = __shfl_sync(0xffffffffu, issued, 0);
       __syncwarp();  // lane 0 has issued every tile: the slot's entries are no longer read
       if (lane == 0) mbar_arrive(&bars->item_empty[q]);
-      it0 += ntiles;
+      it0 += issued;
     }
+    if (lane == 0 && cta_aborted()) drain_ring<kSStages>(bars->full, 0, it0);
   } else {
     // ----------------------------------------------------------- consumers
     for (int j = 0;; ++j) {
       const int q = j & 1;
       StreamSlot& sl = bars->slot[q];
       mbar_wait(&bars->item_full[q], (j >> 1) & 1);
-      const int code = sl.code;
+      // one thread reads the code for all four warps, so they all take the
+      // same branch into merge_store's named barriers even when an aborting
+      // CTA's fetcher rewrites the slot
+      if (threadIdx.x == 0) bars->code_bcast = cta_aborted() ? -1 : sl.code;
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      const int code = bars->code_bcast;
       if (code < 0) break;
       const int split = code & 0xFF, b = code >> 8;
       const int s_begin = split * p.split_tokens;
@@ -611,8 +647,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       if (lane == 0) mbar_arrive(&bars->item_empty[q]);
       float o[16][4];
       float m0, m1, l0, l1;
-      consume_tiles<kFp16, kSStages>(p, smem, bars->full, bars->empty, it0, ntiles, s_begin, s_end, qa, o, m0, m1, l0,
-                                     l1);
+      consume_tiles<kFp16, kSStages>(p, smem, bars->full, bars->empty, &bars->stall, it0, ntiles, s_begin, s_end, qa, o,
+                                     m0, m1, l0, l1);
       merge_store<kFp16>(p, merge_smem, o, m0, m1, l0, l1, nrows, tok0, g, split);
       it0 += ntiles;
     }

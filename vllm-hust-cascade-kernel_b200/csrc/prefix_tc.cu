@@ -70,6 +70,8 @@ struct __align__(8) PrefixBars {
   uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
   uint64_t s_full[2], p_full[2], corr_go[2], o_ready[2];
   uint64_t o_final, fin;
+  uint64_t stall;   // never completed: the debug_stall test hook waits on it
+  uint64_t drain;   // an aborting MMA issuer's last commit
   uint32_t tmem_base;
 };
 static_assert(sizeof(PrefixBars) <= 256, "barrier block");
@@ -214,7 +216,10 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
     }
     mbar_init(&bars->o_final, 1);
     mbar_init(&bars->fin, 128);
+    mbar_init(&bars->stall, 1);
+    mbar_init(&bars->drain, 1);
     fence_mbar_init();
+    cta_wait_init(static_cast<uint64_t>(p.wait_limit_us) * 1000);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
@@ -237,20 +242,29 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
       const int box_rows = bs < kTok ? bs : kTok;
       const int oob_row = p.num_blocks * bs;
       const int x0 = g * kHeadDim;
-      for (int j = 0; j < ntiles; ++j) {
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j, ++issued) {
         const int st = j % kStages, u = j / kStages;
         const int t_tile = s_begin + j * kTok;
         uint8_t* dst = ring + st * kTileBytes;
         if (j >= kStages) mbar_wait(&empty[st], (u - 1) & 1);
+        if (cta_aborted()) break;
         mbar_arrive_expect_tx(&full[st], kTileBytes);
         for (int off = 0; off < kTok; off += box_rows) {
           const int t = t_tile + off;
           const int page = t / bs;
-          const int row = page < npages ? (cached ? btc[page - first_page] : bt[page]) * bs + (t % bs) : oob_row;
+          const int row =
+              page < npages ? paged_row(cached ? btc[page - first_page] : bt[page], t, bs, p.num_blocks, oob_row)
+                            : oob_row;
           tma_load_2d(dst + off * 128, tm, &full[st], x0, row);
           tma_load_2d(dst + kHalf + off * 128, tm, &full[st], x0 + 64, row);
         }
       }
+      // aborting: wait (bounded) for the loads still in flight, the last
+      // kStages issued, before the CTA can exit
+      if (cta_aborted())
+        for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+          mbar_wait_drain(&full[j % kStages], (j / kStages) & 1);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- MMA issuer
@@ -269,6 +283,7 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
           // issued earlier by this thread, so it executes first.
           const int st = j % kStages, u = j / kStages;
           mbar_wait(&bars->k_full[st], u & 1);
+          if (cta_aborted()) break;
           tc_fence_after();
           const uint32_t kb = sK + st * kTileBytes;
 #pragma unroll
@@ -286,6 +301,7 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
           mbar_wait(&bars->v_full[st], u & 1);
           mbar_wait(&bars->p_full[i & 1], (i >> 1) & 1);
           mbar_wait(&bars->o_ready[i & 1], (i >> 1) & 1);
+          if (cta_aborted()) break;
           tc_fence_after();
           const uint32_t vb = sV + st * kTileBytes;
 #pragma unroll
@@ -298,12 +314,18 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
           if (i == ntiles - 1) umma_commit(&bars->o_final);
         }
       }
+      if (cta_aborted()) {
+        // no MMA may still write TMEM (or read shared memory) when it is freed
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
+      }
     }
   } else if (warp < 4) {
     // ---------------------------------------------------------------- softmax
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const float sl2 = p.scale_log2;
     float m = -INFINITY, l = 0.f;
+    if (p.debug_stall) mbar_wait(&bars->stall, 0);  // test hook: runs into the wait limit, the CTA aborts
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1, u = j >> 1;
       const int n_valid = min(kTok, s_end - (s_begin + j * kTok));

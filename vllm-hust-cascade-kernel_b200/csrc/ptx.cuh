@@ -1,11 +1,17 @@
 // Inline-PTX helpers for sm_100a: mbarriers with bounded waits, TMA tensor
 // loads, tcgen05 (TMEM alloc / MMA / ld / commit), ldmatrix and mma.sync.
 //
-// Every wait in this library is bounded: when a spin exceeds its iteration
-// limit the waiting thread records an error code in g_cascade_device_error
-// and carries on, so a broken pipeline ends the kernel with an error status
-// instead of hanging the GPU. The host reads the word back through
-// cascade_device_error().
+// Every wait in this library is bounded in time. When a wait runs past its
+// limit (kWaitLimitNs, 100 ms -- about a thousand times the longest wait a
+// working pipeline has), the waiting thread records kErrMbarTimeout in
+// g_cascade_device_error and raises its CTA's abort flag. From then on every
+// wait in that CTA returns false at once, so all roles run through their
+// remaining loop iterations without blocking, producers stop issuing copies,
+// MMA issuers stop issuing MMAs, and the CTA leaves through its normal
+// teardown: each role first drains what it still has in flight (TMA loads,
+// tensor-core MMAs, bulk stores) with waits that ignore the flag but are
+// bounded themselves, then TMEM is freed. The outputs of an aborted call are
+// garbage; the host reads the error word back through cascade_device_error().
 #pragma once
 
 #include <cuda.h>
@@ -15,7 +21,8 @@
 
 namespace cascade {
 
-// Device error word (bit set = a bounded wait gave up somewhere).
+// Device error word (bit set = a bounded wait gave up somewhere, or a block
+// id outside the pool was met and replaced by a zero-filled page).
 extern __device__ unsigned int g_cascade_device_error;
 
 enum : unsigned int {
@@ -23,10 +30,58 @@ enum : unsigned int {
   kErrBadBlockId = 2u,
 };
 
-// ~2^25 polls of mbarrier.try_wait: each poll suspends for up to the
-// hardware's time limit, so this is several seconds at least -- far beyond
-// any legitimate wait in these kernels (microseconds).
-constexpr uint32_t kSpinLimit = 1u << 25;
+constexpr uint64_t kWaitLimitNs = 100ull * 1000 * 1000;   // one wait
+constexpr uint64_t kDrainLimitNs = 100ull * 1000 * 1000;  // one drain wait after an abort
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Per-CTA wait state in static shared memory: the abort flag and the time
+// limit of one wait. Every kernel that waits on an mbarrier calls
+// cta_wait_init() from one thread before the CTA barrier that precedes its
+// first wait.
+struct CtaWaitState {
+  int abort;
+  int pad;
+  uint64_t limit_ns;
+};
+
+__device__ __forceinline__ CtaWaitState* cta_wait_state() {
+  __shared__ CtaWaitState s_wait_state;
+  return &s_wait_state;
+}
+
+// limit_ns == 0: the default limit.
+__device__ __forceinline__ void cta_wait_init(uint64_t limit_ns = 0) {
+  CtaWaitState* w = cta_wait_state();
+  w->abort = 0;
+  w->limit_ns = limit_ns ? limit_ns : kWaitLimitNs;
+}
+
+__device__ __forceinline__ bool cta_aborted() {
+  return *reinterpret_cast<volatile int*>(&cta_wait_state()->abort) != 0;
+}
+
+__device__ __forceinline__ void cta_abort(unsigned int err) {
+  *reinterpret_cast<volatile int*>(&cta_wait_state()->abort) = 1;
+  atomicOr(&g_cascade_device_error, err);
+}
+
+// Pool row of logical token t of a paged sequence: page id * block_size +
+// in-page row, or `oob_row` (a row past the pool: TMA zero-fills the box)
+// for a block id outside [0, num_blocks). A bad id is recorded as
+// kErrBadBlockId (the caller's table broke the paging contract); the page
+// then reads as zeros instead of another request's KV.
+__device__ __forceinline__ int paged_row(int32_t id, int t, int bs, int num_blocks, int oob_row) {
+  if (static_cast<uint32_t>(id) >= static_cast<uint32_t>(num_blocks)) {
+    atomicOr(&g_cascade_device_error, kErrBadBlockId);
+    return oob_row;
+  }
+  return id * bs + (t % bs);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,14 +119,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete. Returns false
-// (and flags the device error word) if the limit is hit.
+// Bounded wait for the phase with the given parity to complete. Returns
+// false when the CTA is aborting: this wait ran past the limit (it then
+// raises the abort flag and the device error bit) or another thread of the
+// CTA already gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15) == 0) {
+      if (cta_aborted()) return false;
+      if (globaltimer_ns() - t0 >= cta_wait_state()->limit_ns) {
+        cta_abort(kErrMbarTimeout);
+        return false;
+      }
+    }
   }
-  atomicOr(&g_cascade_device_error, kErrMbarTimeout);
-  return false;
+}
+
+// Teardown wait of an aborting CTA for its own asynchronous work (a TMA load
+// or an MMA commit it issued): ignores the abort flag, bounded by
+// kDrainLimitNs. Returns false if the limit ran out.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15) == 15 && globaltimer_ns() - t0 >= kDrainLimitNs) {
+      atomicOr(&g_cascade_device_error, kErrMbarTimeout);
+      return false;
+    }
+  }
 }
 
 // ----------------------------------------------- programmatic launch ----
@@ -293,22 +371,45 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on a barrier of this CTA that the other CTA (or a commit it
-// issued) completes.
+// issued) completes; the same abort rule as mbar_wait (the flag is this
+// CTA's: the other CTA of the pair runs into its own limit).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    if (ok) return true;
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 15) == 0) {
+      if (cta_aborted()) return false;
+      if (globaltimer_ns() - t0 >= cta_wait_state()->limit_ns) {
+        cta_abort(kErrMbarTimeout);
+        return false;
+      }
+    }
   }
-  atomicOr(&g_cascade_device_error, kErrMbarTimeout);
-  return false;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 15) == 15 && globaltimer_ns() - t0 >= kDrainLimitNs) {
+      atomicOr(&g_cascade_device_error, kErrMbarTimeout);
+      return false;
+    }
+  }
 }
 
 // 2-D TMA load into this CTA's shared memory, completing on rank 0's
