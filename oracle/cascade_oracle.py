@@ -118,6 +118,43 @@ def _neighbours(ls, dtype):
 
 
 # ---------------------------------------------------------------------------
+# seeded inputs of the reference's precision suite
+# ---------------------------------------------------------------------------
+
+def gen_paged_inputs(batch, kv_seqlens, num_heads, kv_heads, embed=128, seed=0, q_len=1, block_cols=None,
+                     share_blocks=False):
+    """The seeded paged-KV inputs of the reference's precision suite.
+
+    Restates gen_inputs (fa_fp32_stage1/test/fa_fp32_ref.py:30-60): one
+    numpy default_rng(seed) draws K then V ([num_blocks, 128, KVH, D]) then
+    Q ([batch*q_len, H, D]) from the standard normal in float32; block size
+    128; share_blocks gives every request block ids 0..n-1 (the cascade's
+    shared prefix), otherwise requests get consecutive distinct blocks.
+    Returns (q, k, v float32, block_table int32, q_seqlens int64,
+    kv_seqlens int64, num_tokens)."""
+    rng = np.random.default_rng(seed)
+    kv_seqlens = list(kv_seqlens)
+    bs = 128
+    pages = [(kv + bs - 1) // bs for kv in kv_seqlens]
+    if block_cols is None:
+        block_cols = max(pages)
+    num_blocks = max(pages) if share_blocks else sum(pages)
+    k = rng.standard_normal((num_blocks, bs, kv_heads, embed)).astype(np.float32)
+    v = rng.standard_normal((num_blocks, bs, kv_heads, embed)).astype(np.float32)
+    q = rng.standard_normal((batch * q_len, num_heads, embed)).astype(np.float32)
+    bt = np.zeros((batch, block_cols), dtype=np.int32)
+    nxt = 0
+    for b, nb in enumerate(pages):
+        if share_blocks:
+            bt[b, :nb] = np.arange(nb, dtype=np.int32)
+        else:
+            bt[b, :nb] = np.arange(nxt, nxt + nb, dtype=np.int32)
+            nxt += nb
+    qs = np.full(batch, q_len, dtype=np.int64)
+    return q, k, v, bt, qs, np.asarray(kv_seqlens, dtype=np.int64), int(qs.sum())
+
+
+# ---------------------------------------------------------------------------
 # paged attention (stage-1 shared prefix, and per-request suffix decode)
 # ---------------------------------------------------------------------------
 

@@ -12,7 +12,13 @@ It imports, unmodified, the reference's CPU goldens
   * ascend-kernel/csrc/ops/add_rms_norm_stats/test/add_rms_norm_stats_cases.py
     and add_rms_norm_stats_ref.py (make_inputs, cpu_ref)
 runs them on small seeded cases and writes their inputs/outputs to
-``tests/golden/*.npz``.  It also copies, from the reference's device
+``tests/golden/*.npz``.  For the reference's precision suite
+(fa_fp32_stage1/test/run_precision_suite.py:19-37: 15 shapes x seeds 0, 1,
+read from that file's text because it imports the NPU runtime) it stores,
+per case and seed, a SHA-256 fingerprint of the inputs the reference's own
+gen_inputs draws (bf16 q/k/v bytes, block table, seqlens) and the fp64
+golden's LSE and per-row O sums (fa_fp64_ref), so the full-size inputs can
+be regenerated on the GPU box by the restated generator and checked there.  It also copies, from the reference's device
 self-check record add_rms_norm_stats/test/f2_golden_selfcheck.json, the
 per-element dumps (row, col, fp64 golden, CANN's value and rstd, gamma) and
 the per-case error statistics into
@@ -78,6 +84,69 @@ def make_stage1(ref_dir, out_dir):
             H=H, KVH=KVH, q_len=qlen,
             o_ref=o, lse_ref=lse, A_tb=A.astype(np.float32))
         print("stage1", name, "T", T, "blocks", k.shape[0])
+
+
+def precision_suite_cases(ref_dir):
+    """CASES and SEEDS of run_precision_suite.py, parsed from its text (never
+    executed): literals, lists/tuples of them and list * int."""
+    import ast
+
+    def value(n):
+        if isinstance(n, ast.Constant):
+            return n.value
+        if isinstance(n, (ast.List, ast.Tuple)):
+            items = [value(e) for e in n.elts]
+            return items if isinstance(n, ast.List) else tuple(items)
+        if isinstance(n, ast.BinOp) and isinstance(n.op, ast.Mult):
+            a, b = value(n.left), value(n.right)
+            if isinstance(a, list) and isinstance(b, int):
+                return a * b
+        raise ValueError(f"unexpected expression in the case list: {ast.dump(n)[:80]}")
+
+    path = os.path.join(ref_dir, "ascend-kernel/csrc/ops/fa_fp32_stage1/test/run_precision_suite.py")
+    tree = ast.parse(open(path).read())
+    found = {}
+    for node in tree.body:
+        if isinstance(node, ast.Assign) and len(node.targets) == 1 and isinstance(node.targets[0], ast.Name):
+            if node.targets[0].id in ("CASES", "SEEDS"):
+                found[node.targets[0].id] = value(node.value)
+    return found["CASES"], found["SEEDS"]
+
+
+def input_fingerprint(q16, k16, v16, bt, qs, kvs):
+    import hashlib
+    h = hashlib.sha256()
+    for a in (q16.view(np.uint16), k16.view(np.uint16), v16.view(np.uint16), np.asarray(bt, np.int32),
+              np.asarray(qs, np.int64), np.asarray(kvs, np.int64)):
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def make_precision_suite(ref_dir, out_dir):
+    import json
+    sys.path.insert(0, os.path.join(ref_dir, "ascend-kernel/csrc/ops/fa_fp32_stage1/test"))
+    import fa_fp32_ref as R  # the reference's own golden module
+    cases, seeds = precision_suite_cases(ref_dir)
+    out, meta = {}, {"source": "ascend-kernel/csrc/ops/fa_fp32_stage1/test/run_precision_suite.py:19-37",
+                     "fields": ["name", "batch", "kv_seqlens", "H", "KVH", "q_len", "block_cols_extra"],
+                     "cases": [list(c) for c in cases], "seeds": list(seeds), "sha256": {}}
+    for (name, batch, kvs, H, KVH, qlen, extra) in cases:
+        for seed in seeds:
+            # exactly as run_case() draws them (run_precision_suite.py:47-51)
+            cols = None if extra == 0 else max((kv + 127) // 128 for kv in kvs) + extra
+            q, k, v, bt, qs, kvarr, T = R.gen_inputs(batch, kvs, H, KVH, 128, seed=seed, q_len=qlen,
+                                                   block_cols=cols, share_blocks=True)
+            q16, k16, v16 = R.to_bf16_bytes(q), R.to_bf16_bytes(k), R.to_bf16_bytes(v)
+            key = f"{name}|{seed}"
+            meta["sha256"][key] = input_fingerprint(q16, k16, v16, bt, qs, kvarr)
+            o, lse = R.fa_fp64_ref(q16.astype(np.float64), k16.astype(np.float64), v16.astype(np.float64),
+                                   bt, qs, kvarr, 128, H, KVH)
+            out[key + "|lse"] = lse
+            out[key + "|o_rowsum"] = o.sum(axis=2)
+            print("precision suite", key, "T", T, "blocks", k.shape[0])
+    np.savez_compressed(os.path.join(out_dir, "precision_suite_golden.npz"), **out)
+    with open(os.path.join(out_dir, "precision_suite.json"), "w") as f:
+        json.dump(meta, f, indent=1)
 
 
 def make_merge(ref_dir, out_dir):
@@ -179,9 +248,15 @@ def make_norm(ref_dir, out_dir):
 def main():
     ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     out_dir = os.path.dirname(os.path.abspath(__file__))
-    make_stage1(ref_dir, out_dir)
-    make_merge(ref_dir, out_dir)
-    make_norm(ref_dir, out_dir)
+    only = sys.argv[2:]  # optional subset: stage1 merge norm precision
+    if not only or "stage1" in only:
+        make_stage1(ref_dir, out_dir)
+    if not only or "merge" in only:
+        make_merge(ref_dir, out_dir)
+    if not only or "norm" in only:
+        make_norm(ref_dir, out_dir)
+    if not only or "precision" in only:
+        make_precision_suite(ref_dir, out_dir)
 
 
 if __name__ == "__main__":

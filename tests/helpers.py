@@ -118,3 +118,58 @@ def bits_to_f64(bits, dtype):
     if dtype == "bf16":
         return O.bf16_bits_to_f64(bits)
     return np.asarray(bits, dtype=np.uint16).view(np.float16).astype(np.float64)
+
+
+def _step_oracle_head(item):
+    """Process-pool worker: the fp64 cascade step of one kv head, from the
+    per-head .npy files written by step_oracle_all_heads."""
+    d, g, meta = item
+    ld = lambda n: np.load(os.path.join(d, n))
+    dt = meta["p_dtype"]
+    conv = (lambda b: O.bf16_bits_to_f64(b)) if dt == "bf16" else \
+        (lambda b: np.asarray(b, np.uint16).view(np.float16).astype(np.float64))
+    q = conv(ld(f"q{g}.npy"))
+    k = conv(ld(f"k{g}.npy"))[:, :, None, :]
+    v = conv(ld(f"v{g}.npy"))[:, :, None, :]
+    out, lse = O.cascade_step_ref(q, k, v, ld("bt_p.npy"), meta["group_sizes"], meta["prefix_lens"],
+                                  ld("bt_s.npy"), ld("suf.npy"), p_dtype=dt, out_dtype=meta["out_dtype"],
+                                  round_suffix=meta["round_suffix"])
+    return g, out, lse
+
+
+def step_oracle_all_heads(w, out_dtype="fp32", round_suffix=False):
+    """The CPU oracle of a whole cascade step (oracle.cascade_step_ref) on
+    EVERY kv head of workload ``w``, one spawned worker per kv head; each
+    worker reads only its head's slice of q and of the pools from a temporary
+    directory. Returns (out [B, H, D], lse [B, H])."""
+    import multiprocessing as mp
+    import shutil
+    import tempfile
+    import torch
+    H, KVH = w.q.shape[1], w.k_pool.shape[2]
+    grp = H // KVH
+    p_dtype = "fp16" if w.q.dtype == torch.float16 else "bf16"
+    bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    d = tempfile.mkdtemp(prefix="cascade_oracle_")
+    try:
+        for g in range(KVH):
+            np.save(os.path.join(d, f"q{g}.npy"), bits(w.q[:, g * grp:(g + 1) * grp]))
+            np.save(os.path.join(d, f"k{g}.npy"), bits(w.k_pool[:, :, g]))
+            np.save(os.path.join(d, f"v{g}.npy"), bits(w.v_pool[:, :, g]))
+        np.save(os.path.join(d, "bt_p.npy"), w.tables.prefix_block_table.cpu().numpy())
+        np.save(os.path.join(d, "bt_s.npy"), w.tables.suffix_block_table.cpu().numpy())
+        np.save(os.path.join(d, "suf.npy"), np.asarray(w.suffix_lens))
+        meta = dict(p_dtype=p_dtype, out_dtype=out_dtype, round_suffix=round_suffix,
+                    group_sizes=[int(x) for x in w.group_sizes], prefix_lens=[int(x) for x in w.prefix_lens])
+        workers = max(1, min(KVH, os.cpu_count() or 1))
+        with mp.get_context("spawn").Pool(workers) as pool:
+            res = pool.map(_step_oracle_head, [(d, g, meta) for g in range(KVH)], chunksize=1)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    B = w.q.shape[0]
+    out = np.zeros((B, H, w.q.shape[2]))
+    lse = np.zeros((B, H))
+    for g, o, l in res:
+        out[:, g * grp:(g + 1) * grp] = o
+        lse[:, g * grp:(g + 1) * grp] = l
+    return out, lse
