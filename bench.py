@@ -40,6 +40,9 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "vllm-hust-cascade-kernel_b200"))
 
 METRIC = "cascade decode attention HBM GB/s (Llama-3-8B cascade step, B=64, prefix 4096)"
+# config.workload, byte-identical in both arms
+WORKLOAD = ("c2_llama3_8b_cascade: B=64, shared prefix 4096, suffix U[128,1024], H=32/KVH=8 per rank, D=128, "
+            "block_size=128")
 FLUSH_BYTES = 256 * 1024 * 1024
 LAYERS = 8          # distinct per-layer q/K/V sets the timed steps rotate through
 STEP_KERNELS = 3    # suffix decode + stage-1 + combine
@@ -312,6 +315,12 @@ def run_ours(args, rank, world, local):
 
     verify = verify_sharded(args, rank, world, outs[0]) if world > 1 else None
     del graph
+    torch.cuda.empty_cache()
+
+    c4 = c4_sharded_block(args, peaks, rank, world, K) if not args.no_extra else None
+    c5 = c5_block(peaks, K) if (world == 1 and not args.no_extra) else None
+    roof = read_roof_block(peaks, achieved) if (world == 1 and not args.no_extra) else None
+    hostwall = host_wall_block() if (world == 1 and not args.no_extra) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -332,8 +341,7 @@ def run_ours(args, rank, world, local):
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, random-permutation block tables)",
         "config": {
-            "workload": "c2_llama3_8b_cascade: B=64, shared prefix 4096, suffix U[128,1024], "
-                        "H=32/KVH=8 per rank, D=128, block_size=128",
+            "workload": WORKLOAD,
             "suffix_tokens": int(w.suffix_lens.sum()),
             "algorithmic_bytes_per_step_per_rank": ab,
             "parallelism": f"kv-head partition x{world} (weak: 8 kv heads per rank)",
@@ -382,6 +390,10 @@ def run_ours(args, rank, world, local):
     if norm is not None:
         line["add_rms_norm_stats"] = norm
         line["gpu_launches"] += norm.pop("_launches")
+    for key, blk in (("c4_sharded", c4), ("c5_ragged", c5), ("hbm_read_roof", roof), ("eager_host_wall", hostwall)):
+        if blk is not None:
+            line["gpu_launches"] += blk.pop("_launches")
+            line[key] = blk
     if cpu is not None:
         line["cpu_baseline"] = cpu
     if verify is not None:
@@ -429,6 +441,196 @@ def verify_sharded(args, rank, world, out_local):
         res["gateup_equal_to_single_gpu"] = mlp_ok
     dist.barrier()
     return res
+
+
+def _time_graph(graph, K, stream):
+    """Average device time (ms) of K back-to-back replays of a step graph."""
+    import torch
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    for _ in range(K):
+        graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / K
+
+
+def c5_block(peaks, K, seed=0):
+    """BASELINE config 5, the ragged stress case (N=1): 32 prefix groups of 16
+    requests, prefixes lognormal(median 1024, sigma 1) in [16, 32768], suffixes
+    lognormal(median 200, sigma 1) with 5% forced to 0, H=40/KVH=8, bs=16, fp16.
+    One step (suffix decode, stage-1, combine) captured in a graph and replayed
+    K times back to back (the pools are ~0.8 GB, far above the L2)."""
+    import numpy as np
+    import torch
+    from cascade_kernel import workloads
+    from cascade_kernel.cascade import CascadeStepGraph
+    w = workloads.c5_ragged(seed=seed)
+    g = CascadeStepGraph(w.q, w.k_pool, w.v_pool, w.tables)
+    for _ in range(3):
+        g.replay()
+    ms = _time_graph(g, K, torch.cuda.current_stream())
+    ab = w.algorithmic_bytes()
+    gbs = ab["total"] / (ms * 1e-3) / 1e9
+    suf = np.asarray(w.suffix_lens)
+    del g
+    return {"shape": "c5_ragged: 32 groups x 16 requests, prefix lognormal(ln 1024, 1.0) clipped [16, 32768], "
+                     "suffix lognormal(ln 200, 1.0) with 5% zeros, H=40/KVH=8, D=128, block_size=16, fp16",
+            "sigma_prefix": 1.0, "sigma_suffix": 1.0, "group_split": "16 requests per group", "zero_fraction":
+            round(float((suf == 0).mean()), 4), "prefix_tokens": int(sum(w.prefix_lens)),
+            "suffix_tokens": int(suf.sum()), "algorithmic_bytes_per_step": ab, "us_per_step": round(ms * 1e3, 2),
+            "gbs": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "_launches": 3 * K}
+
+
+def c4_sharded_block(args, peaks, rank, world, K, seed=0):
+    """BASELINE config 4's attention, ONE Llama-3-70B-shaped model (4 prefix
+    groups x 64 requests, 16384-token prefixes, suffix U[256,2048], 64 q / 8 kv
+    heads, bf16) partitioned by kv head over the N ranks: rank r runs its
+    8/N kv heads and their q heads (sharding.shard_attention), tables
+    replicated, no collective in the step. The step is captured in a graph and
+    replayed K times; the time is the max over ranks. Strong scaling: the
+    same model at every N. After timing, NCCL all_gather of the rank outputs,
+    checked bit for bit on rank 0 against the unsharded step, which rank 0
+    also times (T1) in the same run."""
+    import torch
+    from cascade_kernel import sharding, workloads
+    from cascade_kernel.cascade import CascadeStepGraph, cascade_decode
+    stream = torch.cuda.current_stream()
+    w = workloads.c4_llama70b(seed=seed)
+    ab, fl = w.algorithmic_bytes(), w.flops()
+    q, k, v = sharding.shard_attention(w.q, w.k_pool, w.v_pool, rank, world)
+    full = None
+    if rank == 0:
+        full = cascade_decode(w.q, w.k_pool, w.v_pool, w.tables)
+        t1_graph = CascadeStepGraph(w.q, w.k_pool, w.v_pool, w.tables)
+        for _ in range(3):
+            t1_graph.replay()
+        t1_ms = _time_graph(t1_graph, K, stream)
+        del t1_graph
+    if world > 1 or rank != 0:
+        w.q = w.k_pool = w.v_pool = None
+    torch.cuda.empty_cache()
+    g = CascadeStepGraph(q, k, v, w.tables)
+    for _ in range(3):
+        g.replay()
+    barrier(world)
+    ms = max_over_ranks(_time_graph(g, K, stream), world)
+    out = g.replay()
+    torch.cuda.synchronize()
+    res = {"shape": "c4_llama3_70b attention: 4 groups x 64 requests, prefix 16384, suffix U[256,2048], "
+                    f"H=64/KVH=8 split by kv head over {world} rank(s) ({8 // world} kv heads each), bf16",
+           "scaling": "strong (one model, kv heads split across ranks)", "ranks": world,
+           "us_per_step": round(ms * 1e3, 2), "algorithmic_bytes_per_step_all_ranks": ab,
+           "flops_per_step_all_ranks": fl,
+           "gbs_aggregate": round(ab["total"] / (ms * 1e-3) / 1e9, 1),
+           "tflops_aggregate": round(fl["total"] / (ms * 1e-3) / 1e12, 1),
+           "frac_hbm_per_gpu": round(ab["total"] / world / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+           "_launches": 3 * K * (2 if rank == 0 else 1)}
+    if world > 1:
+        import torch.distributed as dist
+        gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device="cuda")
+        dist.all_gather_into_tensor(gathered, out.contiguous())
+        torch.cuda.synchronize()
+        if rank == 0:
+            B, Hr, D = out.shape
+            assembled = gathered.permute(1, 0, 2, 3).reshape(B, world * Hr, D)
+            res["nccl_all_gather_equal_to_unsharded"] = bool(torch.equal(assembled, full))
+        dist.barrier()
+    elif rank == 0:
+        res["equal_to_unsharded"] = bool(torch.equal(out, full))
+    if rank == 0:
+        res["us_per_step_unsharded_1gpu"] = round(t1_ms * 1e3, 2)
+        res["strong_scaling_efficiency"] = round(t1_ms / (world * ms), 4)
+    del g, q, k, v, full
+    torch.cuda.empty_cache()
+    return res
+
+
+def read_roof_block(peaks, dom_gbs, reps=10, gib=2):
+    """The HBM read roof on this GPU: cascade_probe_hbm_read over a 2 GiB
+    buffer (far above the L2) in its three modes -- plain 16-byte loads, the
+    bulk-copy engine, and the decode kernel's paged 2-D TMA pattern without
+    its math (rows of 8 kv heads x 256 bytes, one head's slice per CTA
+    item) -- each timed over `reps` back-to-back launches."""
+    import torch
+    from cascade_kernel import capi
+    buf = torch.empty(gib << 30, dtype=torch.uint8, device="cuda")
+    buf.random_(0, 255)
+    sink = torch.zeros(2048, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+    res = {}
+    for mode, name in ((0, "plain_loads"), (1, "bulk_copy"), (2, "paged_tma_no_math")):
+        for _ in range(2):
+            capi.probe_hbm_read(buf, mode, 2048, sink)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(reps):
+            capi.probe_hbm_read(buf, mode, 2048, sink)
+        b.record(stream)
+        torch.cuda.synchronize()
+        gbs = buf.numel() / (a.elapsed_time(b) / reps * 1e-3) / 1e9
+        res[name] = {"gbs": round(gbs, 1), "frac_of_copy_peak": round(gbs / peaks["hbm_gbs"], 4)}
+    best = max(v["gbs"] for v in res.values())
+    del buf
+    torch.cuda.empty_cache()
+    return {"what": "read-only streaming of a 2 GiB buffer (cascade_probe_hbm_read), 10 back-to-back launches "
+                    "per mode", "per_mode": res, "best_read_gbs": best,
+            "decode_kernel_frac_of_best_read": round(dom_gbs / best, 4),
+            "decode_kernel_frac_of_paged_pattern": round(dom_gbs / res["paged_tma_no_math"]["gbs"], 4),
+            "_launches": 3 * (reps + 2)}
+
+
+def host_wall_block(reps=300, seed=3):
+    """Eager host wall of the reference's ops at the shapes its README quotes
+    host walls for (ascend-kernel/README.md:315-317; method of
+    fa_fp32_stage1/test/run_perf_driver.py:49-60: 10 warm-up calls, then
+    `reps` calls back to back, one synchronize, wall / reps): fa_fp32_stage1
+    fast path at T=64 query tokens of one prefix group, kv=4356, H=40/KVH=8,
+    bf16; lse_merge at B=64 x H=40 x 128 (o1 fp32 padded-LSE, o2 bf16,
+    out_code=1). Device time per call (CUDA events around the same loop) is
+    reported beside it."""
+    import numpy as np
+    import torch
+    npu = torch.ops.npu
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    T, H, KVH, kv = 64, 40, 8, 4356
+    pages = (kv + 127) // 128
+    perm = np.random.default_rng(seed).permutation(pages + 5).astype(np.int32)
+    bt = torch.from_numpy(perm[:pages].reshape(1, pages).copy()).cuda()
+    q = torch.randn(T, H, 128, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(pages + 5, 128, KVH, 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(pages + 5, 128, KVH, 128, device="cuda", generator=g).to(torch.bfloat16)
+    qs = torch.tensor([T], dtype=torch.int64, device="cuda")
+    kvs = torch.tensor([kv], dtype=torch.int64, device="cuda")
+    o1, l1 = npu.fa_fp32_stage1(q, k, v, bt, qs, kvs, T)
+    B = 64
+    o1m = torch.randn(B, H, 128, device="cuda", generator=g)
+    o2m = torch.randn(B, H, 128, device="cuda", generator=g).to(torch.bfloat16)
+    l1m = torch.randn(B * H, 1, device="cuda", generator=g).repeat(1, 8).reshape(-1)
+    l2m = torch.randn(B * H, device="cuda", generator=g)
+    calls = {"fa_fp32_stage1_fast_T64_kv4356_h40_kvh8": lambda: npu.fa_fp32_stage1(q, k, v, bt, qs, kvs, T),
+             "lse_merge_b64_h40_d128_out_code1": lambda: npu.lse_merge(o1m, o2m, l1m, l2m, 1)}
+    published = {"fa_fp32_stage1_fast_T64_kv4356_h40_kvh8": "133.9-135.6 us (910B2, README.md:315)",
+                 "lse_merge_b64_h40_d128_out_code1": "25.4-33.6 us (910B, README.md:317)"}
+    res = {}
+    for name, fn in calls.items():
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) / reps
+        res[name] = {"host_wall_us": round(wall * 1e6, 2), "device_us": round(a.elapsed_time(b) / reps * 1e3, 2),
+                     "reference_published_host_wall": published[name]}
+    return {"method": "run_perf_driver.py:49-60: 10 warm-up calls, then %d eager calls back to back, one "
+                      "synchronize, wall / calls" % reps, "per_op": res, "_launches": 2 * (reps + 10)}
 
 
 def norm_sweep(flush, peaks, reps=5, seed=5):
@@ -551,14 +753,52 @@ def cpu_baseline(w, threads=None, kv_heads=None):
             "seconds": round(wall, 3)}
 
 
+def reference_c2_inputs(seed=0, device="cpu"):
+    """The C2 workload for the reference arm, built without the repo's package
+    (no native library of ours is loaded on that arm): the same recipe as
+    cascade_kernel.workloads.c2_llama8b -- numpy default_rng(seed) draws the
+    64 suffix lengths U[128,1024] and, from a fresh default_rng(seed), the
+    random permutation that places the 32 prefix pages then each request's
+    suffix pages in the pool; a torch generator seeded with `seed` on `device`
+    draws K, V ([pages, 128, 8, 128]) then q ([64, 32, 128]) from N(0,1) in
+    fp32, cast to bf16. Returns an object with the fields cpu_baseline reads."""
+    import types
+    import numpy as np
+    import torch
+    B, H, KVH, D, bs, prefix = 64, 32, 8, 128, 128, 4096
+    suf = np.random.default_rng(seed).integers(128, 1025, size=B).astype(np.int64)
+    rng = np.random.default_rng(seed)
+    pre_pages = prefix // bs
+    suf_pages = [(int(x) + bs - 1) // bs for x in suf]
+    n_pages = pre_pages + sum(suf_pages)
+    perm = rng.permutation(n_pages).astype(np.int32)
+    bt_p = perm[:pre_pages].reshape(1, pre_pages).copy()
+    bt_s = np.zeros((B, max(suf_pages)), np.int32)
+    c = pre_pages
+    for b in range(B):
+        bt_s[b, :suf_pages[b]] = perm[c:c + suf_pages[b]]
+        c += suf_pages[b]
+    gen = torch.Generator(device=device).manual_seed(seed)
+    k = torch.randn((n_pages, bs, KVH, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+    v = torch.randn((n_pages, bs, KVH, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+    q = torch.randn((B, H, D), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+    kvb = 2 * KVH * D * 2
+    total = (2 * B * H * D + prefix * kvb + B * H * D * 4 + B * H * 8 * 4) + \
+        (2 * B * H * D + int(suf.sum()) * kvb + 2 * B * H * D + B * H * 4) + \
+        (B * H * D * 4 + 2 * B * H * D + B * H * 8 * 4 + B * H * 4 + 2 * B * H * D)
+    w = types.SimpleNamespace(q=q, k_pool=k, v_pool=v, group_sizes=[B], prefix_lens=[prefix], suffix_lens=suf,
+                              tables=types.SimpleNamespace(prefix_block_table=torch.from_numpy(bt_p),
+                                                           suffix_block_table=torch.from_numpy(bt_s)))
+    w.algorithmic_bytes = lambda: {"total": total}
+    return w
+
+
 def run_reference(args, rank, world):
     import torch
     if rank != 0:
         return None
-    sys.path.insert(0, os.path.join(ROOT, "vllm-hust-cascade-kernel_b200"))
-    from cascade_kernel import workloads
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    w = workloads.c2_llama8b(seed=args.seed, device=dev)
+    w = reference_c2_inputs(seed=args.seed, device=dev)
     threads = args.cpu_threads or os.cpu_count() or 1
     vals, secs = [], []
     for i in range(args.warmup + args.steps):
@@ -570,7 +810,8 @@ def run_reference(args, rank, world):
     return {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * sum(secs) / len(secs), 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic (seeded)", "config": {"workload": "c2_llama3_8b_cascade (same as ours)"},
+            "data": "synthetic (seeded N(0,1) q/k/v, random-permutation block tables)",
+            "config": {"workload": WORKLOAD},
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": c["cores"], "kind": "port",
                              "sample": c["sample"]},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -587,6 +828,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gateup", action="store_true",
                     help="skip the gate_up SwiGLU and add_rms_norm_stats sweeps")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the C4 sharded, C5 ragged, read-roof and host-wall blocks")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -214,6 +214,19 @@ CASCADE_API int cascade_add_rms_norm_stats(const void *x1, const void *x2, const
 CASCADE_API int cascade_suffix_decode_noalloc(const cascade_paged_attn_t *p, void *out, float *lse,
                                               cascade_stream_t stream);
 
+/* Read-only HBM streaming probe, the read roof of the memory-bound kernels
+ * (the role of the reference's bandwidth probe op, ascend-kernel/csrc/register.cpp:32-33;
+ * interface of its own). Reads `bytes` of device memory at `src` (256-byte
+ * aligned) once and folds them into `sink` (device uint32, at least 1184
+ * words; its contents are meaningless). mode 0: plain 16-byte loads, 8 in
+ * flight per thread, 4 x 148 CTAs of 512 threads; mode 1: 32 KB bulk copies
+ * into a 4-stage shared-memory ring, one CTA per SM; mode 2: the decode
+ * kernel's paged pattern without its math -- rows of `row_bytes` (a multiple
+ * of 256: kv heads x 256 bytes), one kv head's 256-byte slice of 64-row tiles
+ * per 2-D TMA stage, 512-row items, two CTAs per SM. Time it with events. */
+CASCADE_API int cascade_probe_hbm_read(const void *src, size_t bytes, int32_t mode, int64_t row_bytes, uint32_t *sink,
+                                       size_t sink_words, cascade_stream_t stream);
+
 /* Last error message of this thread ("" if none). */
 CASCADE_API const char *cascade_last_error(void);
 

@@ -35,3 +35,20 @@ def test_copy_groups_invariants(n_buf, n_steps, io_group):
         assert 1 <= len(grp) <= limit
         assert len({bufs[i] for i in grp}) == len(grp)
     assert len(g[0]) == 1 and len(g[-1]) == 1
+
+
+def test_reference_arm_inputs_equal_the_workload():
+    """bench.py's reference arm builds the C2 inputs without the repo's package
+    (so none of our native libraries load there); its restated recipe must
+    give the workload our arm times, value for value."""
+    import torch
+    import bench
+    from cascade_kernel import workloads
+    a = bench.reference_c2_inputs(seed=0, device="cpu")
+    b = workloads.c2_llama8b(seed=0, device="cpu")
+    for x, y in ((a.q, b.q), (a.k_pool, b.k_pool), (a.v_pool, b.v_pool),
+                 (a.tables.prefix_block_table, b.tables.prefix_block_table),
+                 (a.tables.suffix_block_table, b.tables.suffix_block_table)):
+        assert torch.equal(x, y.cpu())
+    assert (a.suffix_lens == b.suffix_lens).all()
+    assert a.algorithmic_bytes()["total"] == b.algorithmic_bytes()["total"]

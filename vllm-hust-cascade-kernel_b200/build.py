@@ -25,7 +25,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
 CU_SOURCES = ["capi.cu", "paged_decode.cu", "prefix_tc.cu", "combine.cu", "lse_merge.cu", "gateup.cu", "noalloc.cu",
-              "rms_norm.cu"]
+              "rms_norm.cu", "roofline_probe.cu"]
 HEADERS = ["ptx.cuh", "kernels.h"]
 
 NVCC_FLAGS = [

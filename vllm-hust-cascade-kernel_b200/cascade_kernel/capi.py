@@ -29,6 +29,7 @@ EXPORTED = [
     "cascade_version",
     "cascade_plan_paged_attn",
     "cascade_check_block_table",
+    "cascade_probe_hbm_read",
 ]
 
 
@@ -106,6 +107,8 @@ def load():
     lib.cascade_plan_paged_attn.restype = ctypes.c_int
     lib.cascade_check_block_table.argtypes = [vp, i64, i64, vp, i64, i64, ctypes.POINTER(i64), ctypes.POINTER(i64)]
     lib.cascade_check_block_table.restype = ctypes.c_int
+    lib.cascade_probe_hbm_read.argtypes = [vp, sz, i32, i64, vp, sz, vp]
+    lib.cascade_probe_hbm_read.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -191,6 +194,16 @@ def check_block_table(bt, kv_lens, block_size, num_blocks):
         err = CascadeError(rc, load().cascade_last_error().decode())
         err.bad = (r.value, c.value)
         raise err
+
+
+def probe_hbm_read(src, mode, row_bytes=0, sink=None, stream=None):
+    """cascade_probe_hbm_read over the bytes of device tensor ``src``."""
+    import torch
+    if sink is None:
+        sink = torch.zeros(2048, dtype=torch.int32, device=src.device)
+    return check(load().cascade_probe_hbm_read(
+        _ptr(src), src.numel() * src.element_size(), int(mode), int(row_bytes), _ptr(sink), sink.numel(),
+        stream_ptr(stream)))
 
 
 def stream_ptr(stream=None):
