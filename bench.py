@@ -817,6 +817,13 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def _jsonable(x):
+    """numpy scalars (workload sizes) in the JSON line."""
+    if hasattr(x, "item"):
+        return x.item()
+    raise TypeError(f"not JSON serializable: {type(x).__name__}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -837,12 +844,12 @@ def main():
     if args.impl == "reference":
         line = run_reference(args, rank, world)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line, default=_jsonable), flush=True)
         return
     rank, world, local = setup_dist()
     line = run_ours(args, rank, world, local)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, default=_jsonable), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
