@@ -549,10 +549,11 @@ def c4_sharded_block(args, peaks, rank, world, K, seed=0):
 
 def read_roof_block(peaks, dom_gbs, reps=10, gib=2):
     """The HBM read roof on this GPU: cascade_probe_hbm_read over a 2 GiB
-    buffer (far above the L2) in its three modes -- plain 16-byte loads, the
+    buffer (far above the L2) in its four modes -- plain 16-byte loads, the
     bulk-copy engine, and the decode kernel's paged 2-D TMA pattern without
-    its math (rows of 8 kv heads x 256 bytes, one head's slice per CTA
-    item) -- each timed over `reps` back-to-back launches."""
+    its math (rows of 8 kv heads x 256 bytes, one head's slice per CTA item),
+    items in row-major and in kv-head-major order -- each timed over `reps`
+    back-to-back launches."""
     import torch
     from cascade_kernel import capi
     buf = torch.empty(gib << 30, dtype=torch.uint8, device="cuda")
@@ -560,7 +561,8 @@ def read_roof_block(peaks, dom_gbs, reps=10, gib=2):
     sink = torch.zeros(2048, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
     res = {}
-    for mode, name in ((0, "plain_loads"), (1, "bulk_copy"), (2, "paged_tma_no_math")):
+    for mode, name in ((0, "plain_loads"), (1, "bulk_copy"), (2, "paged_tma_no_math"),
+                       (3, "paged_tma_no_math_head_major")):
         for _ in range(2):
             capi.probe_hbm_read(buf, mode, 2048, sink)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -579,7 +581,7 @@ def read_roof_block(peaks, dom_gbs, reps=10, gib=2):
                     "per mode", "per_mode": res, "best_read_gbs": best,
             "decode_kernel_frac_of_best_read": round(dom_gbs / best, 4),
             "decode_kernel_frac_of_paged_pattern": round(dom_gbs / res["paged_tma_no_math"]["gbs"], 4),
-            "_launches": 3 * (reps + 2)}
+            "_launches": 4 * (reps + 2)}
 
 
 def host_wall_block(reps=300, seed=3):

@@ -223,7 +223,9 @@ CASCADE_API int cascade_suffix_decode_noalloc(const cascade_paged_attn_t *p, voi
  * into a 4-stage shared-memory ring, one CTA per SM; mode 2: the decode
  * kernel's paged pattern without its math -- rows of `row_bytes` (a multiple
  * of 256: kv heads x 256 bytes), one kv head's 256-byte slice of 64-row tiles
- * per 2-D TMA stage, 512-row items, two CTAs per SM. Time it with events. */
+ * per 2-D TMA stage, 512-row items, two CTAs per SM; mode 3: mode 2 with the
+ * items in kv-head-major order (no two CTAs read the same rows at once).
+ * Time it with events. */
 CASCADE_API int cascade_probe_hbm_read(const void *src, size_t bytes, int32_t mode, int64_t row_bytes, uint32_t *sink,
                                        size_t sink_words, cascade_stream_t stream);
 

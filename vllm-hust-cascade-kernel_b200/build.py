@@ -40,8 +40,12 @@ def build(force=False, jobs=8, verbose=False):
     if force and os.path.isdir(BUILD_DIR):
         shutil.rmtree(BUILD_DIR)
     os.makedirs(BUILD_DIR, exist_ok=True)
+    # the host compiler torch's extensions are built with (the system g++):
+    # the torch op library throws c10 errors through libstdc++ code it shares
+    # with torch, so both must use the same C++ runtime
+    cxx = shutil.which("g++") or "g++"
     cfg = ["cmake", "-S", HERE, "-B", BUILD_DIR, "-G", "Ninja", "-DCMAKE_BUILD_TYPE=Release",
-           f"-DCMAKE_CUDA_COMPILER={NVCC}",
+           f"-DCMAKE_CUDA_COMPILER={NVCC}", f"-DCMAKE_CXX_COMPILER={cxx}", f"-DCMAKE_CUDA_HOST_COMPILER={cxx}",
            "-DTORCH_INCLUDE_DIRS=" + ";".join(ce.include_paths()),
            "-DTORCH_LIB_DIR=" + ce.library_paths()[0],
            f"-DCXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}"]

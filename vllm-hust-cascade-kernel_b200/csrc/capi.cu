@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -105,6 +106,25 @@ void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens
     *split_tokens = ceil_div(ceil_div(cap, ns), kTcTile) * kTcTile;
   }
   *num_splits = ceil_div(cap, *split_tokens);
+}
+
+// The fused step's prefix-first rule: when the stage-1 grid has few (request,
+// kv head, 128-row tile) units, splits are chosen so that about
+// kPrefixFirstCtas CTAs of stage-1 run first, concurrently with the suffix
+// decode on the remaining SMs. Measured on the C2 step (16 units): 2 splits
+// (32 CTAs) 39.3 us, 4 splits 41.1 us, 1 split 64.7 us (stage-1 becomes the
+// long pole); larger stage-1 grids (C4: 128 units, C5: 256) keep the
+// decode-first order, where stage-1 needs most SMs anyway.
+constexpr int64_t kPrefixFirstCtas = 32;
+constexpr int64_t kPrefixFirstMaxUnits = 24;
+bool prefix_first_splits(const cascade_paged_attn_t* p, int64_t* splits) {
+  if (p->q_seqlen_value <= 0) return false;
+  const int64_t group = p->num_heads / p->kv_heads;
+  const int64_t units = p->kv_heads * p->batch * ceil_div(p->q_seqlen_value * group, 128);
+  if (units > kPrefixFirstMaxUnits) return false;
+  const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
+  *splits = std::min(ceil_div(kPrefixFirstCtas, units), ceil_div(cap, kTcTile));
+  return true;
 }
 
 // Partials [nsplit][rows][128] fp32 + LSE [nsplit][rows]; a planned decode
@@ -280,6 +300,7 @@ int prepare_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, cu
   L->lse_stride = suffix ? 1 : 8;
   L->partial_out = (p->flags & CASCADE_FLAG_PARTIALS_ONLY) ? 1 : 0;
   L->debug_stall = (p->flags & CASCADE_FLAG_DEBUG_STALL) ? 1 : 0;
+
   L->wait_limit_us = L->debug_stall ? 1000u : 0u;
   L->scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(kHeadDim)) * 1.4426950408889634);
   return CASCADE_OK;
@@ -482,6 +503,20 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
   set_partials(&La, workspace, pa.kernel);
   set_partials(&Lb, static_cast<uint8_t*>(workspace) + need_a, pb.kernel);
   const bool fp16 = suffix->dtype == CASCADE_FP16;
+  // Prefix-first schedule (a small stage-1 grid, e.g. the Llama-3-8B step):
+  // stage-1 runs first on about kPrefixFirstCtas SMs with fewer, longer
+  // splits, and the suffix decode is its programmatic dependent on the other
+  // SMs, so the shared prefix is read while the suffixes stream instead of
+  // after them (C2 step 43.7 -> 39.3 us against the decode-first order).
+  int64_t pf_splits = 0;
+  const bool prefix_first = pa.num_splits && pa.kernel == 1 && pb.num_splits &&
+                            prefix_first_splits(&a, &pf_splits);
+  if (prefix_first) {
+    const int64_t cap = std::max<int64_t>(1, a.block_cols * a.block_size);
+    La.split_tokens = static_cast<int32_t>(ceil_div(ceil_div(cap, pf_splits), kTcTile) * kTcTile);
+    La.num_splits = static_cast<int32_t>(ceil_div(cap, La.split_tokens));
+    set_partials(&La, workspace, pa.kernel);
+  }
   if ((pa.num_splits ? La.num_splits : 0) + (pb.num_splits ? Lb.num_splits : 0) > 64)
     return fail(CASCADE_ERR_UNSUPPORTED, "%s: more than 64 KV splits per row", op);
   cudaError_t e = cudaSuccess;
@@ -490,9 +525,15 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
   // ragged tail drains instead of waiting for the whole grid, and the combine
   // is the programmatic dependent of stage-1 (each kernel's CTAs wait for the
   // kernel before them only when they exit; the combine waits at its start).
-  if (pb.num_splits) e = launch_attention(Lb, pb.kernel, fp16, st);
-  La.pdl = pb.num_splits ? 1 : 0;
-  if (e == cudaSuccess && pa.num_splits) e = launch_attention(La, pa.kernel, fp16, st);
+  if (prefix_first) {
+    e = launch_attention(La, pa.kernel, fp16, st);
+    Lb.pdl = 2;  // only its last CTA waits for stage-1: no slot is held while stage-1 runs
+    if (e == cudaSuccess) e = launch_attention(Lb, pb.kernel, fp16, st);
+  } else {
+    if (pb.num_splits) e = launch_attention(Lb, pb.kernel, fp16, st);
+    La.pdl = pb.num_splits ? 1 : 0;
+    if (e == cudaSuccess && pa.num_splits) e = launch_attention(La, pa.kernel, fp16, st);
+  }
   if (e == cudaSuccess) {
     CascadeCombineLaunch C;
     std::memset(&C, 0, sizeof(C));

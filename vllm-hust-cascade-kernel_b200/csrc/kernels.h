@@ -32,9 +32,11 @@ struct PagedAttnLaunch {
   int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
   int32_t lse_stride;   // 8 (reference padded rows) or 1 (compact)
   int32_t partial_out;  // 1: always write split partials (a later combine produces the output)
-  int32_t pdl;          // 1: launched as a programmatic dependent of the previous kernel in the stream
+  int32_t pdl;          // launched as a programmatic dependent of the previous kernel in the stream:
+                        // 1 = every CTA waits for it before exiting, 2 = only the grid's last CTA does
   int32_t debug_stall;  // 1 (test hook): the consumers first wait on a barrier nothing completes
   uint32_t wait_limit_us;  // limit of one mbarrier wait (0 = the default, kWaitLimitNs)
+
   float scale_log2;     // softmax scale * log2(e)
   // planned decode (kernel 2): workspace arrays after the partials, or null
   int32_t* plan_items;     // [batch * num_splits] (request << 8) | split of the non-empty items

@@ -485,7 +485,11 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
   uint8_t* smem = decode_smem();
   DecodeBarriers* bars = reinterpret_cast<DecodeBarriers*>(smem + kStages * kStageBytes);
   paged_decode_item<kFp16>(p, smem, bars, blockIdx.x, blockIdx.y, blockIdx.z, 0u, true);
-  if (p.pdl && threadIdx.x == 0) pdl_wait();
+  // pdl 1: every CTA waits for the primary before exiting; pdl 2: only the
+  // grid's last CTA does (enough for "this grid completed => the primary
+  // completed" without holding every slot while a long primary runs)
+  const bool last = blockIdx.x == gridDim.x - 1 && blockIdx.y == gridDim.y - 1 && blockIdx.z == gridDim.z - 1;
+  if ((p.pdl == 1 || (p.pdl == 2 && last)) && threadIdx.x == 0) pdl_wait();
 }
 
 // Streaming form of the planned decode, three roles:

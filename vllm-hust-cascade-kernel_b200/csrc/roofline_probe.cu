@@ -13,7 +13,9 @@
 //           and a CTA streams one kv head's 256-byte slice of 64-row tiles
 //           with 2-D TMA boxes [64 rows x 64 x 16-bit] (two per 128 dims,
 //           128-byte swizzle, L2 evict-first) into a 3-stage ring, two CTAs
-//           per SM, work items (kv head, 512 rows) taken in order.
+//           per SM, work items (kv head, 512 rows) taken in order;
+//   mode 3  mode 2 with the items ordered kv head first, so no two CTAs read
+//           the same rows at once (the DRAM-locality contrast to mode 2).
 // Every probe folds what it reads into one word per CTA (written to `sink`),
 // so no load can be dropped. All waits are bounded (ptx.cuh).
 #include <cuda_runtime.h>
@@ -129,6 +131,7 @@ constexpr int kPagedSmem = kPagedStages * kPagedStage + 1024 + 256;
 struct PagedProbe {
   CUtensorMap tmap;      // [rows, heads * 128] 16-bit, box {64, 64}, SW128
   int32_t rows, heads;
+  int32_t head_major;    // mode 3: items ordered kv head first (no two CTAs read the same rows at once)
   uint32_t* sink;
 };
 
@@ -158,7 +161,8 @@ __global__ void __launch_bounds__(64, 2) read_paged_kernel(const __grid_constant
       const uint64_t pol = policy_evict_first();
       uint32_t it = 0;
       for (int item = blockIdx.x; item < items && !cta_aborted(); item += gridDim.x) {
-        const int g = item % p.heads, r0 = (item / p.heads) * kPagedItemRows;
+        const int g = p.head_major ? item / row_blocks : item % p.heads;
+        const int r0 = (p.head_major ? item % row_blocks : item / p.heads) * kPagedItemRows;
         const int r1 = min(p.rows, r0 + kPagedItemRows);
         for (int r = r0; r < r1; r += kPagedTile, ++it) {
           const int st = it % kPagedStages;
@@ -177,7 +181,7 @@ __global__ void __launch_bounds__(64, 2) read_paged_kernel(const __grid_constant
   } else {
     uint32_t it = 0;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
-      const int r0 = (item / p.heads) * kPagedItemRows;
+      const int r0 = (p.head_major ? item % row_blocks : item / p.heads) * kPagedItemRows;
       const int r1 = min(p.rows, r0 + kPagedItemRows);
       for (int r = r0; r < r1; r += kPagedTile, ++it) {
         const int st = it % kPagedStages;
@@ -218,13 +222,14 @@ extern "C" int cascade_probe_hbm_read(const void* src, size_t bytes, int32_t mod
       read_bulk_kernel<<<kNumSMs, 64, kBulkSmem, st>>>(static_cast<const uint8_t*>(src), chunks, sink);
       e = cudaGetLastError();
     }
-  } else if (mode == 2) {
+  } else if (mode == 2 || mode == 3) {
     if (row_bytes <= 0 || row_bytes % 256 != 0)
       return set_error(CASCADE_ERR_INVALID, "cascade_probe_hbm_read: mode 2 needs row_bytes a multiple of 256");
     PagedProbe p;
     std::memset(&p, 0, sizeof(p));
     p.rows = static_cast<int32_t>(std::min<size_t>(bytes / row_bytes, INT32_MAX));
     p.heads = static_cast<int32_t>(row_bytes / 256);
+    p.head_major = mode == 3 ? 1 : 0;
     p.sink = sink;
     if (!encode_tmap_2d(&p.tmap, src, static_cast<uint64_t>(row_bytes / 2), static_cast<uint64_t>(p.rows),
                         static_cast<uint64_t>(row_bytes), 64, kPagedTile, true, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
@@ -235,7 +240,7 @@ extern "C" int cascade_probe_hbm_read(const void* src, size_t bytes, int32_t mod
       e = cudaGetLastError();
     }
   } else {
-    return set_error(CASCADE_ERR_INVALID, "cascade_probe_hbm_read: mode must be 0, 1 or 2");
+    return set_error(CASCADE_ERR_INVALID, "cascade_probe_hbm_read: mode must be 0, 1, 2 or 3");
   }
   if (e != cudaSuccess) {
     char msg[160];
