@@ -75,16 +75,20 @@ def test_planner_kernel_choice_and_splits():
     p = capi.plan(_desc(num_tokens=64, batch=1, block_cols=32, q_seqlen_value=64), 64, False)
     assert p.kernel == 1 and p.rows_per_group == 256 and p.split_tokens % 128 == 0
     assert p.num_splits * p.split_tokens >= 32 * 128
-    assert (p.split_tokens, p.num_splits) == (512, 8)          # 16 row tiles x 8 splits = 128 CTAs
+    # two-tile form: 8 (kv head, tile pair) units x 16 splits = 128 CTAs
+    assert (p.split_tokens, p.num_splits) == (256, 16)
     # C5-like stage-1 (32 groups x 16 requests, group 5, prefixes up to 4016
     # tokens at bs 16): 256 row tiles fill the SMs already, but the longest
     # prefixes are still cut in two
     p = capi.plan(_desc(num_tokens=512, batch=32, num_heads=40, block_size=16, block_cols=251, q_seqlen_value=16),
                   16, False)
     assert p.kernel == 1 and (p.split_tokens, p.num_splits) == (2048, 2)
-    # C4-like (4 groups x 64 requests, group 8, prefix 16384): 128 row tiles x 2 splits
+    # C4-like (4 groups x 64 requests, group 8, prefix 16384): 64 tile pairs x 2 splits
     p = capi.plan(_desc(num_tokens=256, batch=4, num_heads=64, block_cols=128, q_seqlen_value=64), 64, False)
     assert p.kernel == 1 and (p.split_tokens, p.num_splits) == (8192, 2)
+    # 128 rows or fewer per request: one row tile per CTA, 148 / units splits
+    p = capi.plan(_desc(num_tokens=32, batch=1, num_heads=32, block_cols=32, q_seqlen_value=32), 32, False)
+    assert p.kernel == 1 and (p.split_tokens, p.num_splits) == (256, 16)
     # 16 rows is still the decode path, 17 is not
     assert capi.plan(_desc(num_tokens=5, batch=1, q_seqlen_value=5, num_heads=32), 5, False).kernel == 1
     assert capi.plan(_desc(num_tokens=4, batch=1, q_seqlen_value=4, num_heads=16), 4, False).kernel == 0

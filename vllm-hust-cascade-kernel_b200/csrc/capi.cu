@@ -95,14 +95,24 @@ void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens
     *split_tokens = std::max<int64_t>(kDecodeSplit * widen, ceil_div(ceil_div(cap, kMaxSplits), 64) * 64);
   } else {
     const int64_t group = p->num_heads / p->kv_heads;
-    const int64_t mtiles = std::max<int64_t>(p->batch, ceil_div(p->num_tokens * group, 128));
-    const int64_t units = p->kv_heads * mtiles;
-    // Enough splits for one 225 KB CTA per SM, and at least two: the grid is
-    // sized by the longest request, and on ragged prefixes (C5) the longest
-    // requests' CTAs set the kernel's length (C5 step 297 -> 276 us with two
-    // splits; uniform shapes with >= 148 row tiles lose ~4% to the extra wave).
-    const int64_t want = std::max<int64_t>(2, ceil_div(kNumSMs, units));
-    int64_t ns = std::min<int64_t>(std::min<int64_t>(std::max<int64_t>(want, 1), ceil_div(cap, kTcTile)), kMaxSplits);
+    const int64_t rows_req = p->q_seqlen_value > 0 ? p->q_seqlen_value * group : 0;
+    int64_t want;
+    if (rows_req > 128) {
+      // two-tile form: units = (kv head, pair of 128-row tiles); as many splits
+      // as keep the grid within one wave of one CTA per SM (C4: 64 units x 2
+      // splits = 128 CTAs; 3 splits would run 192 CTAs in two rounds), at least two
+      const int64_t units = p->kv_heads * p->batch * ceil_div(rows_req, 256);
+      want = std::max<int64_t>(2, kNumSMs / std::max<int64_t>(1, units));
+    } else {
+      const int64_t mtiles = std::max<int64_t>(p->batch, ceil_div(p->num_tokens * group, 128));
+      const int64_t units = p->kv_heads * mtiles;
+      // Enough splits for one 225 KB CTA per SM, and at least two: the grid is
+      // sized by the longest request, and on ragged prefixes (C5) the longest
+      // requests' CTAs set the kernel's length (C5 step 297 -> 276 us with two
+      // splits; uniform shapes with >= 148 row tiles lose ~4% to the extra wave).
+      want = std::max<int64_t>(2, ceil_div(kNumSMs, units));
+    }
+    int64_t ns = std::min<int64_t>(std::min<int64_t>(want, ceil_div(cap, kTcTile)), kMaxSplits);
     *split_tokens = ceil_div(ceil_div(cap, ns), kTcTile) * kTcTile;
   }
   *num_splits = ceil_div(cap, *split_tokens);
@@ -120,7 +130,8 @@ constexpr int64_t kPrefixFirstMaxUnits = 24;
 bool prefix_first_splits(const cascade_paged_attn_t* p, int64_t* splits) {
   if (p->q_seqlen_value <= 0) return false;
   const int64_t group = p->num_heads / p->kv_heads;
-  const int64_t units = p->kv_heads * p->batch * ceil_div(p->q_seqlen_value * group, 128);
+  const int64_t rows = p->q_seqlen_value * group;
+  const int64_t units = p->kv_heads * p->batch * ceil_div(rows, rows > 128 ? 256 : 128);
   if (units > kPrefixFirstMaxUnits) return false;
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
   *splits = std::min(ceil_div(kPrefixFirstCtas, units), ceil_div(cap, kTcTile));

@@ -107,6 +107,12 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Stores 32 consecutive output elements of one row (fp32 or 16-bit).
@@ -551,10 +557,397 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
   if (p.pdl && threadIdx.x == 0) pdl_wait();
 }
 
+// ---------------------------------------------------------------------------
+// Two-tile form: one CTA = (KV split, kv head x PAIR of 128-row tiles,
+// request). Both row tiles (A = rows [256 p, 256 p + 128), B = the next 128)
+// read the same K/V tiles, and two softmax warpgroups alternate so that the
+// tensor pipe always has the other tile's MMAs while one softmax runs:
+//   warps 0-3   softmax + epilogue of tile A (thread = row = TMEM lane)
+//   warps 4-7   softmax + epilogue of tile B
+//   warps 8-11  Q staging (both tiles, shared memory), O rescale of both tiles
+//   warp 12     K producer, warp 13 V producer (2-stage rings)
+//   warp 14     MMA issuer (one thread)
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512); P_X over the
+// first 64 columns of S_X. Q_A, Q_B in shared memory (SS MMA for S). Per KV
+// tile j the issue order is PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): S_X(j+1)
+// overwrites P_X(j) only after PV_X(j) (same issuing thread, executed in
+// order). The arithmetic per row tile is the one-tile kernel's (S per 128
+// tokens, running max, P = round16(exp(S - m)), unquantised row sums,
+// O = dm O + P V with the rescale skipped exactly when no row of a warp moved
+// its max), so both forms give the same quantisation structure.
+constexpr int kPpThreads = 16 * 32;
+constexpr int kPpStages = 2;
+constexpr int kPpOffQ = 0;                                    // Q_A, Q_B: 2 x 32 KB
+constexpr int kPpOffK = kPpOffQ + 2 * kTileBytes;             // K ring
+constexpr int kPpOffV = kPpOffK + kPpStages * kTileBytes;     // V ring
+constexpr int kPpOffAux = kPpOffV + kPpStages * kTileBytes;   // dm[2 tiles][2][128], block table
+constexpr int kPpOffBars = kPpOffAux + 4 * 128 * 4 + kBtCache * 4;
+static_assert(kPpOffBars % 16 == 0, "mbarriers need 8-byte alignment");
+constexpr int kPpSmemBytes = kPpOffBars + 512 + 1024;
+static_assert(kPpSmemBytes <= 227 * 1024, "shared memory per CTA");
+constexpr int kPpStagePitch = kHeadDim + 4;                   // fp32 epilogue staging row pitch (floats)
+static_assert(2 * kRows * kPpStagePitch * 4 <= kPpOffAux, "both tiles' epilogue staging fit below the aux area");
+
+struct __align__(8) PpBars {
+  uint64_t q_full;
+  uint64_t k_full[kPpStages], k_empty[kPpStages], v_full[kPpStages], v_empty[kPpStages];
+  uint64_t s_full[2], p_full[2];          // per tile
+  uint64_t corr_go[2][2], o_ready[2][2];  // [tile][j & 1]
+  uint64_t o_final[2];
+  uint64_t stall, drain;
+  uint32_t tmem_base;
+};
+static_assert(sizeof(PpBars) <= 512, "barrier block");
+
+template <bool kFp16>
+__device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* dmbuf = reinterpret_cast<float*>(smem + kPpOffAux);          // [2 tiles][2][128]
+  int32_t* btc = reinterpret_cast<int32_t*>(dmbuf + 4 * kRows);       // [kBtCache]
+  PpBars* bars = reinterpret_cast<PpBars*>(smem + kPpOffBars);
+
+  const int split = blockIdx.x;
+  const int g = blockIdx.y % p.kv_heads;
+  const int mp = blockIdx.y / p.kv_heads;  // row-tile pair
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;
+
+  const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(p.block_cols) * p.block_size));
+  const int q_len = p.q_seqlen_value > 0 ? p.q_seqlen_value : static_cast<int>(p.q_seqlens[b]);
+  const int nrows = q_len * p.group;
+  const int row0[2] = {mp * 2 * kRows, mp * 2 * kRows + kRows};
+  const int unit_rows[2] = {min(kRows, nrows - row0[0]), min(kRows, nrows - row0[1])};
+  const int tok0 = token_offset(p, b);
+  if (unit_rows[0] <= 0) return;  // this request has fewer row tiles
+  const int s_begin = split * p.split_tokens;
+  const int s_end = min(kv, s_begin + p.split_tokens);
+  const int ntiles = s_end > s_begin ? (s_end - s_begin + kTok - 1) / kTok : 0;
+  const size_t plane = static_cast<size_t>(p.num_tokens) * p.num_heads;
+  const bool partial = p.num_splits > 1 || p.partial_out;
+
+  auto out_row = [&](int t, int r) -> size_t {
+    const int rr = row0[t] + r;
+    return static_cast<size_t>(tok0 + rr / p.group) * p.num_heads + g * p.group + rr % p.group;
+  };
+
+  if (ntiles == 0) {
+    // split beyond this request's kv (or kv == 0)
+    for (int i = tid; i < 2 * kRows; i += blockDim.x) {
+      const int t = i / kRows, r = i % kRows;
+      if (r >= unit_rows[t]) continue;
+      const size_t row = out_row(t, r);
+      if (partial) {
+        p.part_lse[static_cast<size_t>(split) * plane + row] = -INFINITY;
+      } else {
+        float* o = static_cast<float*>(p.out) + row * kHeadDim;
+        for (int c = 0; c < kHeadDim; ++c) o[c] = 0.f;
+        for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = -INFINITY;
+      }
+    }
+    return;
+  }
+
+  const int bs = p.block_size;
+  const int32_t* bt = p.block_table + static_cast<size_t>(b) * p.block_cols;
+  const int npages = (kv + bs - 1) / bs;
+  const int first_page = s_begin / bs;
+  const int nbt = min(npages, (s_end + bs - 1) / bs) - first_page;
+  const bool cached = nbt <= kBtCache;
+  if (warp == 12 && cached) {
+    for (int i = lane; i < nbt; i += 32) btc[i] = bt[first_page + i];
+  }
+  if (tid == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kPpStages; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t], 128);
+      mbar_init(&bars->o_final[t], 1);
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(&bars->corr_go[t][s], 129);
+        mbar_init(&bars->o_ready[t][s], 128);
+      }
+    }
+    mbar_init(&bars->stall, 1);
+    mbar_init(&bars->drain, 1);
+    fence_mbar_init();
+    cta_wait_init(static_cast<uint64_t>(p.wait_limit_us) * 1000);
+  }
+  if (warp == 14) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 12 || warp == 13) {
+    // ---------------------------------------------------- K / V producers
+    if (lane == 0) {
+      const bool is_v = warp == 13;
+      const CUtensorMap* tm = is_v ? &p.tmap_v : &p.tmap_k;
+      uint64_t* full = is_v ? bars->v_full : bars->k_full;
+      uint64_t* empty = is_v ? bars->v_empty : bars->k_empty;
+      uint8_t* ring = smem + (is_v ? kPpOffV : kPpOffK);
+      tma_prefetch_desc(tm);
+      const int box_rows = bs < kTok ? bs : kTok;
+      const int oob_row = p.num_blocks * bs;
+      const int x0 = g * kHeadDim;
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j, ++issued) {
+        const int st = j % kPpStages, u = j / kPpStages;
+        if (j >= kPpStages) mbar_wait(&empty[st], (u - 1) & 1);
+        if (cta_aborted()) break;
+        mbar_arrive_expect_tx(&full[st], kTileBytes);
+        uint8_t* dst = ring + st * kTileBytes;
+        for (int off = 0; off < kTok; off += box_rows) {
+          const int t = s_begin + j * kTok + off;
+          const int page = t / bs;
+          const int row =
+              page < npages ? paged_row(cached ? btc[page - first_page] : bt[page], t, bs, p.num_blocks, oob_row)
+                            : oob_row;
+          tma_load_2d(dst + off * 128, tm, &full[st], x0, row);
+          tma_load_2d(dst + kHalf + off * 128, tm, &full[st], x0 + 64, row);
+        }
+      }
+      if (cta_aborted())
+        for (int j = issued > kPpStages ? issued - kPpStages : 0; j < issued; ++j)
+          mbar_wait_drain(&full[j % kPpStages], (j / kPpStages) & 1);
+    }
+  } else if (warp == 14) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t fmt = kFp16 ? 0u : 1u;
+      const uint32_t idesc_s = make_idesc_f16(128, 128, fmt, 0, 0);
+      const uint32_t idesc_pv = make_idesc_f16(128, 128, fmt, 0, 1);
+      const uint32_t sQ = smem_u32(smem + kPpOffQ);
+      const uint32_t sK = smem_u32(smem + kPpOffK);
+      const uint32_t sV = smem_u32(smem + kPpOffV);
+      auto issue_s = [&](int t, int kst) {
+        const uint32_t qb = sQ + t * kTileBytes, kb = sK + kst * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t koff = (k >> 2) * kHalf + (k & 3) * 32;
+          umma_f16_ss(tbase + t * 128, make_smem_desc(qb + koff, 16, 1024, 2), make_smem_desc(kb + koff, 16, 1024, 2),
+                      idesc_s, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->s_full[t]);
+      };
+      auto issue_pv = [&](int t, int vst, int j) {
+        const uint32_t vb = sV + vst * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          umma_f16_ts(tbase + 256 + t * 128, tbase + t * 128 + k * 8, make_smem_desc(vb + k * 2048, kHalf, 1024, 2),
+                      idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+      };
+      mbar_arrive(&bars->corr_go[0][0]);  // tile 0 has no PV_{-1} to wait for
+      mbar_arrive(&bars->corr_go[1][0]);
+      mbar_wait(&bars->q_full, 0);
+      mbar_wait(&bars->k_full[0], 0);
+      tc_fence_after();
+      if (!cta_aborted()) {
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&bars->k_empty[0]);
+      }
+      for (int j = 0; j < ntiles && !cta_aborted(); ++j) {
+        const int vst = j % kPpStages;
+        const bool more = j + 1 < ntiles;
+        const int kst = (j + 1) % kPpStages;
+        mbar_wait(&bars->v_full[vst], (j / kPpStages) & 1);
+        for (int t = 0; t < 2; ++t) {
+          mbar_wait(&bars->p_full[t], j & 1);
+          mbar_wait(&bars->o_ready[t][j & 1], (j >> 1) & 1);
+          if (cta_aborted()) break;
+          tc_fence_after();
+          issue_pv(t, vst, j);
+          if (t == 1) umma_commit(&bars->v_empty[vst]);
+          umma_commit(more ? &bars->corr_go[t][(j + 1) & 1] : &bars->o_final[t]);
+          if (more) {
+            if (t == 0) mbar_wait(&bars->k_full[kst], ((j + 1) / kPpStages) & 1);
+            if (cta_aborted()) break;
+            tc_fence_after();
+            issue_s(t, kst);
+            if (t == 1) umma_commit(&bars->k_empty[kst]);
+          }
+        }
+      }
+      if (cta_aborted()) {
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
+      }
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------- softmax + epilogue, tile t
+    const int t = warp >> 2;
+    const int r = tid & 127;  // row == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t scol = tbase + lane_off + t * 128;
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    if (p.debug_stall && t == 0) mbar_wait(&bars->stall, 0);  // test hook: runs into the wait limit
+    for (int j = 0; j < ntiles; ++j) {
+      const int n_valid = min(kTok, s_end - (s_begin + j * kTok));
+      mbar_wait(&bars->s_full[t], j & 1);
+      tc_fence_after();
+      // pass 1: the tile's row max (16 columns at a time)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t sv[16];
+        tmem_ld_32x32b_x16(scol + c * 16, sv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (c * 16 + e < n_valid) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      }
+      const float m_new = fmaxf(m, mx * sl2);
+      const float dm = (m == -INFINITY) ? 1.f : ex2(m - m_new);
+      dmbuf[(t * 2 + (j & 1)) * kRows + r] = dm;
+      mbar_arrive(&bars->corr_go[t][j & 1]);
+      // pass 2: P = round16(exp(S - m)) over the first 64 columns, row sum of the unrounded exps
+      // (P of columns [16c, 16c + 16) goes to columns [8c, 8c + 8): never over
+      // an S column that a later chunk still reads)
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t sv[16];
+        tmem_ld_32x32b_x16(scol + c * 16, sv);
+        tmem_wait_ld();
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const bool v0 = c * 16 + e < n_valid, v1 = c * 16 + e + 1 < n_valid;
+          const float x0 = v0 ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -m_new)) : 0.f;
+          const float x1 = v1 ? ex2(fmaf(__uint_as_float(sv[e + 1]), sl2, -m_new)) : 0.f;
+          rs += x0 + x1;
+          pk[e >> 1] = pack2<kFp16>(x0, x1);
+        }
+        tmem_st_32x32b_x8(scol + c * 8, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[t]);
+      l = dm * l + rs;
+      m = m_new;
+    }
+    // epilogue of tile t: O / l once its last PV is done, fp32 rows staged in
+    // shared memory (whole 512-byte rows for the bulk-copy engine)
+    mbar_wait(&bars->o_final[t], 0);
+    tc_fence_after();
+    const float inv = 1.f / l;
+    const float lse_nat = (m + __log2f(l)) * 0.6931471805599453f;
+    float* stage = reinterpret_cast<float*>(smem) + t * kRows * kPpStagePitch;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      tmem_ld_32x32b_x32(tbase + lane_off + 256 + t * 128 + c * 32, o);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float4*>(stage + r * kPpStagePitch + c * 32 + i * 4) =
+            make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                        __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (r < unit_rows[t]) {
+      const size_t row = out_row(t, r);
+      float* dst = partial ? p.part_o + (static_cast<size_t>(split) * plane + row) * kHeadDim
+                           : static_cast<float*>(p.out) + row * kHeadDim;
+      bulk_store_1d(dst, stage + r * kPpStagePitch, kHeadDim * 4);
+      bulk_commit_group();
+      if (partial) {
+        p.part_lse[static_cast<size_t>(split) * plane + row] = lse_nat;
+      } else {
+        for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = lse_nat;
+      }
+      bulk_wait_group0();
+    }
+  } else if (warp < 12) {
+    // ----------------------------------- Q staging + O rescale of both tiles
+    const int r = tid - 256;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    {
+      // Q rows -> shared memory in the K tiles' layout ([128 rows][64 x 16-bit]
+      // halves, 128-byte swizzle); rows past the unit are zero
+#pragma unroll 1
+      for (int t = 0; t < 2; ++t) {
+        const bool ok = r < unit_rows[t];
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.query) +
+                                                           out_row(t, ok ? r : 0) * kHeadDim);
+        uint8_t* qt = smem + kPpOffQ + t * kTileBytes;
+#pragma unroll 4
+        for (int c = 0; c < 16; ++c) {
+          const uint4 v = ok ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(qt + (c >> 3) * kHalf + sw128(r, c & 7)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (r == 0) mbar_arrive(&bars->q_full);
+    }
+    for (int j = 0; j < ntiles; ++j) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        mbar_wait(&bars->corr_go[t][j & 1], (j >> 1) & 1);
+        const float dm = dmbuf[(t * 2 + (j & 1)) * kRows + r];
+        if (j >= 1 && __any_sync(0xffffffffu, dm != 1.f)) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            const uint32_t a = tbase + lane_off + 256 + t * 128 + c * 32;
+            tmem_ld_32x32b_x32(a, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * dm);
+            tmem_st_32x32b_x32(a, o);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->o_ready[t][j & 1]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 14) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+template <bool kFp16>
+__global__ void __launch_bounds__(kPpThreads, 1) paged_prefix_pp_kernel(const __grid_constant__ PagedAttnLaunch p) {
+  pdl_launch_dependents();
+  paged_prefix_pp_body<kFp16>(p);
+  if (p.pdl && threadIdx.x == 0) pdl_wait();
+}
+
 }  // namespace
 
 cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStream_t stream) {
   const int mtiles = (p.max_q_seqlen * p.group + kRows - 1) / kRows;
+  if (mtiles >= 2 && (p.num_splits > 1 || p.partial_out || p.out_dtype == 2)) {
+    // two row tiles per CTA (fp32 output or split partials)
+    dim3 grid(p.num_splits, p.kv_heads * ((mtiles + 1) / 2), p.batch);
+    auto kern = fp16 ? paged_prefix_pp_kernel<true> : paged_prefix_pp_kernel<false>;
+    cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kPpSmemBytes);
+    if (e != cudaSuccess) return e;
+    return launch_maybe_pdl(kern, grid, dim3(kPpThreads), kPpSmemBytes, stream, p.pdl != 0, p);
+  }
   dim3 grid(p.num_splits, p.kv_heads * mtiles, p.batch);
   auto kern = fp16 ? paged_prefix_tc_kernel<true> : paged_prefix_tc_kernel<false>;
   cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kSmemBytes);
