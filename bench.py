@@ -456,6 +456,40 @@ def _time_graph(graph, K, stream):
     return a.elapsed_time(b) / K
 
 
+def kernel_times(w, K):
+    """Stage-1 alone and the suffix decode alone on workload w (split
+    partials, no combine: CASCADE_FLAG_PARTIALS_ONLY through the C ABI), each
+    the average of K back-to-back launches in one graph. Returns (stage-1 us,
+    decode us)."""
+    import torch
+    from cascade_kernel import capi
+    t = w.tables
+    res = []
+    for bt, qs, kvs, qv, stage1 in ((t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens, t.uniform_group,
+                                     True),
+                                    (t.suffix_block_table, t.suffix_q_seqlens, t.suffix_kv_seqlens, 1, False)):
+        d = capi.paged_desc(w.q, w.k_pool, w.v_pool, bt, qs, kvs, qv, flags=capi.FLAG_PARTIALS_ONLY)
+        n = capi.stage1_workspace_size(d) if stage1 else capi.suffix_workspace_size(d)
+        ws = torch.empty(max(n, 1), dtype=torch.uint8, device="cuda")
+        fn = (lambda: capi.fa_fp32_stage1(d, None, None, ws)) if stage1 else (lambda: capi.suffix_decode(d, None, None, ws))
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(K):
+                fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        res.append(a.elapsed_time(b) / K * 1e3)
+        del g, ws
+    return res
+
+
 def c5_block(peaks, K, seed=0):
     """BASELINE config 5, the ragged stress case (N=1): 32 prefix groups of 16
     requests, prefixes lognormal(median 1024, sigma 1) in [16, 32768], suffixes
@@ -475,12 +509,15 @@ def c5_block(peaks, K, seed=0):
     gbs = ab["total"] / (ms * 1e-3) / 1e9
     suf = np.asarray(w.suffix_lens)
     del g
+    s1_us, dec_us = kernel_times(w, K)
     return {"shape": "c5_ragged: 32 groups x 16 requests, prefix lognormal(ln 1024, 1.0) clipped [16, 32768], "
                      "suffix lognormal(ln 200, 1.0) with 5% zeros, H=40/KVH=8, D=128, block_size=16, fp16",
             "sigma_prefix": 1.0, "sigma_suffix": 1.0, "group_split": "16 requests per group", "zero_fraction":
             round(float((suf == 0).mean()), 4), "prefix_tokens": int(sum(w.prefix_lens)),
             "suffix_tokens": int(suf.sum()), "algorithmic_bytes_per_step": ab, "us_per_step": round(ms * 1e3, 2),
-            "gbs": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "_launches": 3 * K}
+            "gbs": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+            "stage1_alone_us": round(s1_us, 2), "suffix_decode_alone_us": round(dec_us, 2),
+            "_launches": 5 * K}
 
 
 def c4_sharded_block(args, peaks, rank, world, K, seed=0):
@@ -508,6 +545,7 @@ def c4_sharded_block(args, peaks, rank, world, K, seed=0):
             t1_graph.replay()
         t1_ms = _time_graph(t1_graph, K, stream)
         del t1_graph
+        s1_us, dec_us = kernel_times(w, K)
     if world > 1 or rank != 0:
         w.q = w.k_pool = w.v_pool = None
     torch.cuda.empty_cache()
@@ -526,7 +564,7 @@ def c4_sharded_block(args, peaks, rank, world, K, seed=0):
            "gbs_aggregate": round(ab["total"] / (ms * 1e-3) / 1e9, 1),
            "tflops_aggregate": round(fl["total"] / (ms * 1e-3) / 1e12, 1),
            "frac_hbm_per_gpu": round(ab["total"] / world / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
-           "_launches": 3 * K * (2 if rank == 0 else 1)}
+           "_launches": 3 * K * (2 if rank == 0 else 1) + (2 * K if rank == 0 else 0)}
     if world > 1:
         import torch.distributed as dist
         gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device="cuda")
@@ -541,6 +579,12 @@ def c4_sharded_block(args, peaks, rank, world, K, seed=0):
         res["equal_to_unsharded"] = bool(torch.equal(out, full))
     if rank == 0:
         res["us_per_step_unsharded_1gpu"] = round(t1_ms * 1e3, 2)
+        # the two attention kernels of the unsharded step alone (stage-1: 137.4
+        # GFLOP, tensor-bound; the suffix decode: HBM-bound)
+        res["stage1_alone_us_1gpu"] = round(s1_us, 2)
+        res["stage1_tflops_1gpu"] = round(fl["stage1"] / (s1_us * 1e-6) / 1e12, 1)
+        res["stage1_frac_tensor_1gpu"] = round(fl["stage1"] / (s1_us * 1e-6) / 1e12 / peaks["bf16_tflops"], 4)
+        res["suffix_decode_alone_us_1gpu"] = round(dec_us, 2)
         res["strong_scaling_efficiency"] = round(t1_ms / (world * ms), 4)
     del g, q, k, v, full
     torch.cuda.empty_cache()
