@@ -84,7 +84,7 @@ typedef struct cascade_paged_attn {
  * first wait on a barrier that nothing completes, with a 1 ms limit instead
  * of the default 100 ms. The wait runs out, the CTA aborts (its other waits
  * return at once, producers stop and drain their copies in flight, TMEM is
- * freed) and the call ends with bit 1 of cascade_device_error() set. The
+ * freed) and the call ends with (word & 1) set in cascade_device_error(). The
  * outputs of such a call are garbage. */
 #define CASCADE_FLAG_DEBUG_STALL 2
 
@@ -93,7 +93,7 @@ typedef struct cascade_paged_attn {
  * reject the call with CASCADE_ERR_INVALID if a page a request reads has a
  * block id outside [0, num_blocks) (cascade_check_block_table below). Without
  * it the kernels still never read outside the pool: such a page reads as
- * zeros and bit 2 of cascade_device_error() is set. */
+ * zeros and the word cascade_device_error() reads has (word & 2) set. */
 #define CASCADE_FLAG_CHECK_BLOCK_IDS 4
 
 /* Host-side check of a block table against the paging contract (no CUDA

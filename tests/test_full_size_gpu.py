@@ -6,7 +6,8 @@ heads) and the ragged stress case (C5: 32 groups, lognormal prefixes up to
 32768 tokens, block size 16, fp16, GQA 5, zero-length suffixes).
 
 Checks: the fused single-combine step and the reference consumer's three-op
-chain agree to within the chain's extra rounding and are finite; the CPU
+chain agree to within the chain's extra rounding (plus, on C2, the P-rounding
+structure of the fused step's prefix-first stage-1 splits) and are finite; the CPU
 oracle of the whole step, run on EVERY kv head (one spawned worker per kv
 head), matches the fused step at the BASELINE tolerance (2e-2) and at one
 output ulp plus the P-rounding structure slack."""
@@ -36,7 +37,11 @@ def test_full_size_step(name):
     assert Hh.capi().device_error() == 0
     a, b = Hh.dev_to_f64(fused), Hh.dev_to_f64(chain)
     assert np.isfinite(a).all() and np.isfinite(b).all()
-    bound = O.ulp(np.maximum(np.abs(a), np.abs(b)), dt) + 0.5 * O.ulp(Hh.dev_to_f64(o2), dt) + 1e-7
+    # the chain rounds the suffix partial once more; on C2 the fused step also
+    # runs stage-1 with its prefix-first splits (fewer, longer than the
+    # standalone op's), which moves where P is rounded: the structure slack
+    slack = 2e-3 if name == "c2" else 1e-7
+    bound = O.ulp(np.maximum(np.abs(a), np.abs(b)), dt) + 0.5 * O.ulp(Hh.dev_to_f64(o2), dt) + slack
     assert (np.abs(a - b) <= bound).all(), float((np.abs(a - b) - bound).max())
 
     # the oracle on every kv head

@@ -107,12 +107,6 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
-
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Stores 32 consecutive output elements of one row (fp32 or 16-bit).
@@ -800,40 +794,49 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
       const int n_valid = min(kTok, s_end - (s_begin + j * kTok));
       mbar_wait(&bars->s_full[t], j & 1);
       tc_fence_after();
-      // pass 1: the tile's row max (16 columns at a time)
+      // pass 1: the tile's row max, 64 columns per TMEM round trip
       float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t sv[16];
-        tmem_ld_32x32b_x16(scol + c * 16, sv);
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sa[32], sb[32];
+        tmem_ld_32x32b_x32(scol + h * 64, sa);
+        tmem_ld_32x32b_x32(scol + h * 64 + 32, sb);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (c * 16 + e < n_valid) mx = fmaxf(mx, __uint_as_float(sv[e]));
+        for (int e = 0; e < 32; ++e) {
+          if (h * 64 + e < n_valid) mx = fmaxf(mx, __uint_as_float(sa[e]));
+          if (h * 64 + 32 + e < n_valid) mx = fmaxf(mx, __uint_as_float(sb[e]));
+        }
       }
       const float m_new = fmaxf(m, mx * sl2);
       const float dm = (m == -INFINITY) ? 1.f : ex2(m - m_new);
       dmbuf[(t * 2 + (j & 1)) * kRows + r] = dm;
       mbar_arrive(&bars->corr_go[t][j & 1]);
-      // pass 2: P = round16(exp(S - m)) over the first 64 columns, row sum of the unrounded exps
-      // (P of columns [16c, 16c + 16) goes to columns [8c, 8c + 8): never over
-      // an S column that a later chunk still reads)
+      // pass 2: P = round16(exp(S - m)) over the first 64 columns, row sum of
+      // the unrounded exps; 64 columns per round trip (P of columns
+      // [64h, 64h + 64) goes to [32h, 32h + 32): never over an S column a later
+      // load still reads)
       float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t sv[16];
-        tmem_ld_32x32b_x16(scol + c * 16, sv);
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sa[32], sb[32];
+        tmem_ld_32x32b_x32(scol + h * 64, sa);
+        tmem_ld_32x32b_x32(scol + h * 64 + 32, sb);
         tmem_wait_ld();
-        uint32_t pk[8];
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          const bool v0 = c * 16 + e < n_valid, v1 = c * 16 + e + 1 < n_valid;
-          const float x0 = v0 ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -m_new)) : 0.f;
-          const float x1 = v1 ? ex2(fmaf(__uint_as_float(sv[e + 1]), sl2, -m_new)) : 0.f;
-          rs += x0 + x1;
-          pk[e >> 1] = pack2<kFp16>(x0, x1);
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t(&sv)[32] = q ? sb : sa;
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int c0 = h * 64 + q * 32 + e;
+            const float x0 = c0 < n_valid ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -m_new)) : 0.f;
+            const float x1 = c0 + 1 < n_valid ? ex2(fmaf(__uint_as_float(sv[e + 1]), sl2, -m_new)) : 0.f;
+            rs += x0 + x1;
+            pk[e >> 1] = pack2<kFp16>(x0, x1);
+          }
+          tmem_st_32x32b_x16(scol + h * 32 + q * 16, pk);
         }
-        tmem_st_32x32b_x8(scol + c * 8, pk);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -905,14 +908,19 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
         if (j >= 1 && __any_sync(0xffffffffu, dm != 1.f)) {
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            const uint32_t a = tbase + lane_off + 256 + t * 128 + c * 32;
-            tmem_ld_32x32b_x32(a, o);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t oa[32], ob[32];
+            const uint32_t a = tbase + lane_off + 256 + t * 128 + h * 64;
+            tmem_ld_32x32b_x32(a, oa);
+            tmem_ld_32x32b_x32(a + 32, ob);
             tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * dm);
-            tmem_st_32x32b_x32(a, o);
+            for (int e = 0; e < 32; ++e) {
+              oa[e] = __float_as_uint(__uint_as_float(oa[e]) * dm);
+              ob[e] = __float_as_uint(__uint_as_float(ob[e]) * dm);
+            }
+            tmem_st_32x32b_x32(a, oa);
+            tmem_st_32x32b_x32(a + 32, ob);
           }
           tmem_wait_st();
         }
