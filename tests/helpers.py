@@ -98,6 +98,60 @@ def kernel_structure(q_len, group, kv_cap_tokens, T, H, KVH, batch, block_cols, 
     return 1, dict(chunk=128, split=int(p.split_tokens))
 
 
+def stage1_pieces(q_len, group, KVH, batch, cap_tokens, sms=148, min_run=8):
+    """The equal-run schedule of the two-tile stage-1 (pp_pieces in capi.cu):
+    None when the split grid is used, else a function (b, g, mp) -> list of
+    (first tile, end tile) pieces of that unit, in 128-token KV tiles."""
+    rows = q_len * group
+    if q_len <= 0 or rows <= 128:
+        return None
+    pairs = -(-rows // 256)
+    units = KVH * batch * pairs
+    tc = -(-max(1, cap_tokens) // 128)
+    T = units * tc
+    G = min(sms, T)
+    if G <= units or T < G * min_run:
+        return None
+    starts = sorted(set([c * T // G for c in range(G)] + [T]))
+
+    def pieces(b, g, mp):
+        u = (b * KVH + g) * pairs + mp
+        lo, hi = u * tc, (u + 1) * tc
+        cuts = [lo] + [x for x in starts if lo < x < hi] + [hi]
+        return [(a - lo, e - lo) for a, e in zip(cuts[:-1], cuts[1:])]
+    return pieces
+
+
+def stage1_pieces_oracle(qf, kf, vf, bt, qs, kvs, group, pieces):
+    """Kernel-structured fp64 stage-1 of the equal-run schedule: each (request,
+    kv head, row-tile pair) unit runs the reference recurrence (128-token
+    chunks) separately over each of its pieces, the pieces merged in LSE space
+    -- paged_attention_ref per unit with that unit's segments. Returns (O,
+    LSE, tie-band bound A)."""
+    T, H, D = qf.shape
+    KVH = H // group
+    O_ = np.zeros((T, H, D))
+    L_ = np.full((T, H), -np.inf)
+    A_ = np.zeros((T, H, D))
+    tok = 0
+    for b in range(len(qs)):
+        ql, kv = int(qs[b]), int(kvs[b])
+        tok_per_pair = 256 // group
+        for g in range(KVH):
+            for mp in range(-(-ql * group // 256)):
+                t0, t1 = tok + mp * tok_per_pair, tok + min(ql, (mp + 1) * tok_per_pair)
+                segs = [[np.arange(t * 128, min((t + 1) * 128, kv)) for t in range(a, e) if t * 128 < kv]
+                        for a, e in pieces(b, g, mp)]
+                segs = [s for s in segs if s]
+                hs = slice(g * group, (g + 1) * group)
+                o, l, a = O.paged_attention_ref(qf[t0:t1, hs], kf[:, :, g:g + 1], vf[:, :, g:g + 1], bt[b:b + 1],
+                                                np.array([t1 - t0]), np.array([kv]), segments=lambda _kv: segs,
+                                                with_tieband=True, tieband_rule="rescaled")
+                O_[t0:t1, hs], L_[t0:t1, hs], A_[t0:t1, hs] = o, l, a
+        tok += ql
+    return O_, L_, A_
+
+
 def norm_inputs(m, k, dtype, seed, has_beta):
     """The seeded inputs of add_rms_norm_stats_cases.make_inputs
     (add_rms_norm_stats/test/add_rms_norm_stats_cases.py:33-43), drawn on the

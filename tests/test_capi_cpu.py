@@ -83,9 +83,10 @@ def test_planner_kernel_choice_and_splits():
     p = capi.plan(_desc(num_tokens=512, batch=32, num_heads=40, block_size=16, block_cols=251, q_seqlen_value=16),
                   16, False)
     assert p.kernel == 1 and (p.split_tokens, p.num_splits) == (2048, 2)
-    # C4-like (4 groups x 64 requests, group 8, prefix 16384): 64 tile pairs x 2 splits
+    # C4-like (4 groups x 64 requests, group 8, prefix 16384): 64 tile pairs x 128 tiles cut into 148
+    # equal runs of 55-56 tiles (pieces of at most 56 x 128 tokens; some unit spans 4 runs -> 4 planes)
     p = capi.plan(_desc(num_tokens=256, batch=4, num_heads=64, block_cols=128, q_seqlen_value=64), 64, False)
-    assert p.kernel == 1 and (p.split_tokens, p.num_splits) == (8192, 2)
+    assert p.kernel == 1 and (p.split_tokens, p.num_splits) == (7168, 4)
     # 128 rows or fewer per request: one row tile per CTA, 148 / units splits
     p = capi.plan(_desc(num_tokens=32, batch=1, num_heads=32, block_cols=32, q_seqlen_value=32), 32, False)
     assert p.kernel == 1 and (p.split_tokens, p.num_splits) == (256, 16)

@@ -115,6 +115,32 @@ def _rand_case(B, H, KVH, bs, kv_lens, q_len, dtype, seed, permute=True, cols_ex
     return dev, (qf, kf, vf, bt, qs, kvs)
 
 
+@pytest.mark.parametrize("H,kv_lens", [(32, [9600, 3000]), (64, [9728])], ids=["one_pair_ragged", "two_pairs"])
+def test_stage1_equal_runs_exact_structure(H, kv_lens):
+    """Two-tile stage-1 on the equal-run schedule (units' KV tiles cut into one
+    run per SM, a run spanning two units, a unit's pieces on consecutive
+    planes, pieces past a short prefix empty): against the kernel-structured
+    oracle of exactly those pieces, and the fp64 single pass at the reference
+    tolerance."""
+    Hh.need_cuda()
+    KVH, q_len, bs = 8, 64, 128
+    group = H // KVH
+    dev, (qf, kf, vf, bt, qs, kvs) = _rand_case(len(kv_lens), H, KVH, bs, kv_lens, q_len, "bf16", seed=11)
+    pieces = Hh.stage1_pieces(q_len, group, KVH, len(kv_lens), bt.shape[1] * bs)
+    assert pieces is not None  # the shape takes the equal-run schedule
+    assert max(len(pieces(b, g, mp)) for b in range(len(kv_lens)) for g in range(KVH)
+               for mp in range(q_len * group // 256)) >= 3
+    out, lse = Hh.run_capi_paged(*dev, q_len)
+    o = Hh.dev_to_f64(out)
+    l = Hh.dev_to_f64(lse).reshape(-1, 8)[:, 0].reshape(o.shape[0], H)
+    o_ks, l_ks, A = Hh.stage1_pieces_oracle(qf, kf, vf, bt, qs, kvs, group, pieces)
+    _assert_within(o, o_ks, A + 3e-6)
+    assert np.abs(l - l_ks).max() < 1e-5
+    o_ref, l_ref = O.paged_attention_ref(qf, kf, vf, bt, qs, kvs, chunk=512)
+    assert np.abs(o - o_ref).max() < O_TOL_REF
+    assert np.abs(l - l_ref).max() < LSE_TOL
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 @pytest.mark.parametrize("bs", [16, 32, 64, 128, 256])
 def test_suffix_decode_block_sizes(dtype, bs):

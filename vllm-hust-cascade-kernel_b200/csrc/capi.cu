@@ -79,6 +79,36 @@ bool decode_planned(const cascade_paged_attn_t* p) {
          p->batch * p->kv_heads * ceil_div(cap, kDecodeSplit) > 16384;
 }
 
+// Equal-run schedule of the two-tile stage-1 (uniform q only): the 128-token
+// KV tiles of all (request, kv head, row-tile pair) units, concatenated, are
+// cut into one equal run per SM, so every CTA does the same number of tiles
+// whatever the unit count (C4: 64 units x 128 tiles; the split grid ran 128
+// CTAs of 64 tiles each and left 20 SMs idle). A run may end in one unit and
+// start the next; a unit's pieces go to consecutive partial planes. Used when
+// a run is shorter than a unit and at least kMinRunTiles long (the CTA's
+// pipeline refills at each piece boundary).
+constexpr int64_t kMinRunTiles = 8;
+bool pp_pieces(const cascade_paged_attn_t* p, int64_t* ctas, int64_t* unit_tiles, int64_t* planes) {
+  if (p->q_seqlen_value <= 0) return false;
+  const int64_t rows = p->q_seqlen_value * (p->num_heads / p->kv_heads);
+  if (rows <= 128) return false;
+  const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
+  const int64_t units = p->kv_heads * p->batch * ceil_div(rows, 256);
+  const int64_t tc = ceil_div(cap, kTcTile);
+  const int64_t T = units * tc;
+  const int64_t G = std::min<int64_t>(kNumSMs, T);
+  if (G <= units || T < G * kMinRunTiles) return false;
+  // the CTA whose run [floor(c T / G), floor((c + 1) T / G)) holds tile x
+  auto cta_of = [&](int64_t x) { return ((x + 1) * G + T - 1) / T - 1; };
+  int64_t most = 1;
+  for (int64_t u = 0; u < units; ++u) most = std::max(most, cta_of(u * tc + tc - 1) - cta_of(u * tc) + 1);
+  if (most > kMaxSplits) return false;
+  *ctas = G;
+  *unit_tiles = tc;
+  *planes = most;
+  return true;
+}
+
 // Shape-only split rule of each kernel.
 void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens, int64_t* num_splits) {
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
@@ -94,6 +124,15 @@ void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens
     const int64_t widen = std::min<int64_t>(4, std::max<int64_t>(1, p->batch * p->kv_heads / 1024));
     *split_tokens = std::max<int64_t>(kDecodeSplit * widen, ceil_div(ceil_div(cap, kMaxSplits), 64) * 64);
   } else {
+    int64_t G, tc, planes;
+    if (pp_pieces(p, &G, &tc, &planes)) {
+      // equal runs: the longest piece, and one partial plane per piece of a unit
+      *split_tokens = ceil_div(tc * p->kv_heads * p->batch *
+                                   ceil_div(p->q_seqlen_value * (p->num_heads / p->kv_heads), 256),
+                               G) * kTcTile;
+      *num_splits = planes;
+      return;
+    }
     const int64_t group = p->num_heads / p->kv_heads;
     const int64_t rows_req = p->q_seqlen_value > 0 ? p->q_seqlen_value * group : 0;
     int64_t want;
@@ -307,6 +346,11 @@ int prepare_paged(const cascade_paged_attn_t* p, const char* op, bool suffix, cu
   L->max_q_seqlen = static_cast<int32_t>(max_q);
   L->split_tokens = static_cast<int32_t>(plan->split_tokens);
   L->num_splits = static_cast<int32_t>(plan->num_splits);
+  int64_t pc, put, planes;
+  if (tc && pp_pieces(p, &pc, &put, &planes)) {
+    L->piece_ctas = static_cast<int32_t>(pc);
+    L->piece_unit_tiles = static_cast<int32_t>(put);
+  }
   L->out_dtype = suffix ? p->dtype : CASCADE_FP32;
   L->lse_stride = suffix ? 1 : 8;
   L->partial_out = (p->flags & CASCADE_FLAG_PARTIALS_ONLY) ? 1 : 0;
@@ -526,6 +570,7 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
     const int64_t cap = std::max<int64_t>(1, a.block_cols * a.block_size);
     La.split_tokens = static_cast<int32_t>(ceil_div(ceil_div(cap, pf_splits), kTcTile) * kTcTile);
     La.num_splits = static_cast<int32_t>(ceil_div(cap, La.split_tokens));
+    La.piece_ctas = 0;  // the split grid
     set_partials(&La, workspace, pa.kernel);
   }
   if ((pa.num_splits ? La.num_splits : 0) + (pb.num_splits ? Lb.num_splits : 0) > 64)

@@ -29,6 +29,12 @@ struct PagedAttnLaunch {
   int32_t q_seqlen_value;  // > 0 uniform, 0 = per-request (prefix-summed in kernel)
   int32_t max_q_seqlen;
   int32_t split_tokens, num_splits;
+  // two-tile stage-1 over equal runs of KV tiles (0 = the split grid): the
+  // grid has piece_ctas CTAs; (request, kv head, row-tile pair) units of
+  // piece_unit_tiles 128-token tiles are concatenated and cut into piece_ctas
+  // equal runs, each CTA taking one run (one or two pieces of units); a
+  // piece's partial goes to plane "its index among the unit's pieces"
+  int32_t piece_ctas, piece_unit_tiles;
   int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
   int32_t lse_stride;   // 8 (reference padded rows) or 1 (compact)
   int32_t partial_out;  // 1: always write split partials (a later combine produces the output)

@@ -109,6 +109,16 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Columns [nv, 64) of a 64-column S chunk (two 32-column loads) -> -inf.
+__device__ __forceinline__ void mask_cols(uint32_t (&sa)[32], uint32_t (&sb)[32], int nv) {
+  const uint32_t ninf = __float_as_uint(-INFINITY);
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    sa[e] = e < nv ? sa[e] : ninf;
+    sb[e] = 32 + e < nv ? sb[e] : ninf;
+  }
+}
+
 // Stores 32 consecutive output elements of one row (fp32 or 16-bit).
 __device__ __forceinline__ void store_chunk(const PagedAttnLaunch& p, size_t elem, const uint32_t (&r)[32],
                                             float scale) {
@@ -349,9 +359,15 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
 #pragma unroll
         for (int e = 0; e < kTok; ++e) s[e] = e < n_valid ? s[e] : -INFINITY;
       }
-      float mx = -INFINITY;
+      float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < kTok; ++e) mx = fmaxf(mx, s[e]);
+      for (int e = 0; e < kTok; e += 8) {
+        m0 = fmax3f(m0, s[e], s[e + 1]);
+        m1 = fmax3f(m1, s[e + 2], s[e + 3]);
+        m2 = fmax3f(m2, s[e + 4], s[e + 5]);
+        m3 = fmax3f(m3, s[e + 6], s[e + 7]);
+      }
+      const float mx = fmax3f(m0, m1, fmaxf(m2, m3));
       const float m_new = fmaxf(m, mx * sl2);
       const float dm = (m == -INFINITY) ? 1.f : ex2(m - m_new);
       dmbuf[st * kRows + tid] = dm;
@@ -359,19 +375,26 @@ __device__ __forceinline__ void paged_prefix_tc_body(const PagedAttnLaunch& p) {
       // P_j over the first 64 columns of S_j (already in registers), in two
       // 32-column halves. PV_{j-2}, the last reader of this buffer,
       // completed before S_j did.
-      float rs = 0.f;
+      float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;  // two packed row-sum accumulators
+      const float neg_m = -m_new;
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float x0 = ex2(fmaf(s[q4 * 32 + e], sl2, -m_new));      // masked: ex2(-inf) = 0
-          const float x1 = ex2(fmaf(s[q4 * 32 + e + 1], sl2, -m_new));
-          rs += x0 + x1;
+        for (int e = 0; e < 32; e += 4) {
+          const float* sv = s + q4 * 32 + e;
+          float y0, y1, y2, y3;
+          ffma2_bcast(y0, y1, sv[0], sv[1], sl2, neg_m);
+          ffma2_bcast(y2, y3, sv[2], sv[3], sl2, neg_m);
+          const float x0 = ex2(y0), x1 = ex2(y1), x2 = ex2(y2), x3 = ex2(y3);  // masked: ex2(-inf) = 0
+          fadd2(r0, r1, x0, x1);
+          fadd2(r2, r3, x2, x3);
           pk[e >> 1] = pack2<kFp16>(x0, x1);
+          pk[(e >> 1) + 1] = pack2<kFp16>(x2, x3);
         }
         tmem_st_32x32b_x16(tbase + lane_off + st * 128 + q4 * 16, pk);
       }
+      const float rs = (r0 + r1) + (r2 + r3);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_full[st]);
@@ -559,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
 //   warps 0-3   softmax + epilogue of tile A (thread = row = TMEM lane)
 //   warps 4-7   softmax + epilogue of tile B
 //   warps 8-11  Q staging (both tiles, shared memory), O rescale of both tiles
-//   warp 12     K producer, warp 13 V producer (2-stage rings)
+//   warp 12     K producer (2-slot ring), warp 13 V producer (3-slot ring)
 //   warp 14     MMA issuer (one thread)
 // TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512); P_X over the
 // first 64 columns of S_X. Q_A, Q_B in shared memory (SS MMA for S). Per KV
@@ -570,41 +593,58 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefix_tc_kernel(const __gr
 // O = dm O + P V with the rescale skipped exactly when no row of a warp moved
 // its max), so both forms give the same quantisation structure.
 constexpr int kPpThreads = 16 * 32;
-constexpr int kPpStages = 2;
+// K slots free after S_B(j + 1) and are next needed by S_A(j + 3); V slots
+// free after PV_B(j) and are next needed by PV_A(j + 3): the third V slot
+// gives the V loads the same lookahead as the K loads (with two, PV_A waited
+// for V on long prefixes).
+constexpr int kPpKStages = 2;
+constexpr int kPpVStages = 3;
+constexpr int kPpBtCache = 128;
 constexpr int kPpOffQ = 0;                                    // Q_A, Q_B: 2 x 32 KB
 constexpr int kPpOffK = kPpOffQ + 2 * kTileBytes;             // K ring
-constexpr int kPpOffV = kPpOffK + kPpStages * kTileBytes;     // V ring
-constexpr int kPpOffAux = kPpOffV + kPpStages * kTileBytes;   // dm[2 tiles][2][128], block table
-constexpr int kPpOffBars = kPpOffAux + 4 * 128 * 4 + kBtCache * 4;
+constexpr int kPpOffV = kPpOffK + kPpKStages * kTileBytes;    // V ring
+constexpr int kPpOffAux = kPpOffV + kPpVStages * kTileBytes;  // dm[2 tiles][128], block table
+constexpr int kPpOffBars = kPpOffAux + 2 * 128 * 4 + kPpBtCache * 4;
 static_assert(kPpOffBars % 16 == 0, "mbarriers need 8-byte alignment");
-constexpr int kPpSmemBytes = kPpOffBars + 512 + 1024;
-static_assert(kPpSmemBytes <= 227 * 1024, "shared memory per CTA");
+constexpr int kPpSmemBytes = kPpOffBars + 256 + 1024;
+// static shared memory (the 16-byte wait state) counts against the same limit
+static_assert(kPpSmemBytes + 16 <= 227 * 1024, "shared memory per CTA");
 constexpr int kPpStagePitch = kHeadDim + 4;                   // fp32 epilogue staging row pitch (floats)
 static_assert(2 * kRows * kPpStagePitch * 4 <= kPpOffAux, "both tiles' epilogue staging fit below the aux area");
 
 struct __align__(8) PpBars {
   uint64_t q_full;
-  uint64_t k_full[kPpStages], k_empty[kPpStages], v_full[kPpStages], v_empty[kPpStages];
+  uint64_t k_full[kPpKStages], k_empty[kPpKStages], v_full[kPpVStages], v_empty[kPpVStages];
   uint64_t s_full[2], p_full[2];          // per tile
   uint64_t corr_go[2][2], o_ready[2][2];  // [tile][j & 1]
   uint64_t o_final[2];
   uint64_t stall, drain;
   uint32_t tmem_base;
 };
-static_assert(sizeof(PpBars) <= 512, "barrier block");
+static_assert(sizeof(PpBars) <= 256, "barrier block");
+constexpr int kPpNumBars = static_cast<int>(offsetof(PpBars, tmem_base) / sizeof(uint64_t));
 
+// One piece of a two-tile CTA's work: request b, kv head g, row-tile pair mp
+// against KV tokens [s_begin, min(kv_b, s_lim)), written as split-partial
+// plane `split` (or as the final output when the call has one split and no
+// partials). fill_to > split + 1: this CTA holds the unit's last piece, and
+// planes (split, fill_to) of the unit's rows get -inf LSEs. The barriers are
+// (re)initialised here (bars_live: they hold a previous piece's state and
+// are invalidated first); TMEM is allocated by the caller. All threads call
+// it; it returns whether the barriers are initialised, after a CTA barrier
+// when it used them.
 template <bool kFp16>
-__device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* dmbuf = reinterpret_cast<float*>(smem + kPpOffAux);          // [2 tiles][2][128]
-  int32_t* btc = reinterpret_cast<int32_t*>(dmbuf + 4 * kRows);       // [kBtCache]
+__device__ __forceinline__ bool paged_prefix_pp_piece(const PagedAttnLaunch& p, uint8_t* smem, uint32_t tbase,
+                                                      int b, int g, int mp, int split, int s_begin, int s_lim,
+                                                      int fill_to, bool bars_live) {
+  // dm of tile t's current KV tile: written by the softmax (pass 1 of tile
+  // j), read by the rescale before it releases PV(j); the next write (tile
+  // j + 1) needs S(j + 1), which is issued after PV(j), so one slot per
+  // row tile suffices
+  float* dmbuf = reinterpret_cast<float*>(smem + kPpOffAux);          // [2 tiles][128]
+  int32_t* btc = reinterpret_cast<int32_t*>(dmbuf + 2 * kRows);       // [kPpBtCache]
   PpBars* bars = reinterpret_cast<PpBars*>(smem + kPpOffBars);
 
-  const int split = blockIdx.x;
-  const int g = blockIdx.y % p.kv_heads;
-  const int mp = blockIdx.y / p.kv_heads;  // row-tile pair
-  const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
@@ -615,9 +655,8 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
   const int row0[2] = {mp * 2 * kRows, mp * 2 * kRows + kRows};
   const int unit_rows[2] = {min(kRows, nrows - row0[0]), min(kRows, nrows - row0[1])};
   const int tok0 = token_offset(p, b);
-  if (unit_rows[0] <= 0) return;  // this request has fewer row tiles
-  const int s_begin = split * p.split_tokens;
-  const int s_end = min(kv, s_begin + p.split_tokens);
+  if (unit_rows[0] <= 0) return bars_live;  // this request has fewer row tiles
+  const int s_end = min(kv, s_lim);
   const int ntiles = s_end > s_begin ? (s_end - s_begin + kTok - 1) / kTok : 0;
   const size_t plane = static_cast<size_t>(p.num_tokens) * p.num_heads;
   const bool partial = p.num_splits > 1 || p.partial_out;
@@ -626,6 +665,14 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
     const int rr = row0[t] + r;
     return static_cast<size_t>(tok0 + rr / p.group) * p.num_heads + g * p.group + rr % p.group;
   };
+
+  // planes past the unit's last piece hold no work
+  for (int i = tid; i < 2 * kRows && fill_to > split + 1; i += blockDim.x) {
+    const int t = i / kRows, r = i % kRows;
+    if (r >= unit_rows[t]) continue;
+    const size_t row = out_row(t, r);
+    for (int sl = split + 1; sl < fill_to; ++sl) p.part_lse[static_cast<size_t>(sl) * plane + row] = -INFINITY;
+  }
 
   if (ntiles == 0) {
     // split beyond this request's kv (or kv == 0)
@@ -641,7 +688,7 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
         for (int c = 0; c < p.lse_stride; ++c) p.lse[row * p.lse_stride + c] = -INFINITY;
       }
     }
-    return;
+    return bars_live;
   }
 
   const int bs = p.block_size;
@@ -649,15 +696,21 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
   const int npages = (kv + bs - 1) / bs;
   const int first_page = s_begin / bs;
   const int nbt = min(npages, (s_end + bs - 1) / bs) - first_page;
-  const bool cached = nbt <= kBtCache;
+  const bool cached = nbt <= kPpBtCache;
   if (warp == 12 && cached) {
     for (int i = lane; i < nbt; i += 32) btc[i] = bt[first_page + i];
   }
   if (tid == 0) {
+    if (bars_live) {
+      uint64_t* all = reinterpret_cast<uint64_t*>(bars);
+      for (int i = 0; i < kPpNumBars; ++i) mbar_inval(all + i);
+    }
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < kPpStages; ++s) {
+    for (int s = 0; s < kPpKStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < kPpVStages; ++s) {
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
@@ -673,16 +726,10 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
     mbar_init(&bars->stall, 1);
     mbar_init(&bars->drain, 1);
     fence_mbar_init();
-    cta_wait_init(static_cast<uint64_t>(p.wait_limit_us) * 1000);
-  }
-  if (warp == 14) {
-    tmem_alloc(&bars->tmem_base, kTmemCols);
-    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tbase = bars->tmem_base;
 
   if (warp == 12 || warp == 13) {
     // ---------------------------------------------------- K / V producers
@@ -696,10 +743,11 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
       const int box_rows = bs < kTok ? bs : kTok;
       const int oob_row = p.num_blocks * bs;
       const int x0 = g * kHeadDim;
+      const int stages = is_v ? kPpVStages : kPpKStages;
       int issued = 0;
       for (int j = 0; j < ntiles; ++j, ++issued) {
-        const int st = j % kPpStages, u = j / kPpStages;
-        if (j >= kPpStages) mbar_wait(&empty[st], (u - 1) & 1);
+        const int st = j % stages, u = j / stages;
+        if (j >= stages) mbar_wait(&empty[st], (u - 1) & 1);
         if (cta_aborted()) break;
         mbar_arrive_expect_tx(&full[st], kTileBytes);
         uint8_t* dst = ring + st * kTileBytes;
@@ -714,8 +762,8 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
         }
       }
       if (cta_aborted())
-        for (int j = issued > kPpStages ? issued - kPpStages : 0; j < issued; ++j)
-          mbar_wait_drain(&full[j % kPpStages], (j / kPpStages) & 1);
+        for (int j = issued > stages ? issued - stages : 0; j < issued; ++j)
+          mbar_wait_drain(&full[j % stages], (j / stages) & 1);
     }
   } else if (warp == 14) {
     // ------------------------------------------------------------- MMA issuer
@@ -755,10 +803,10 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
         umma_commit(&bars->k_empty[0]);
       }
       for (int j = 0; j < ntiles && !cta_aborted(); ++j) {
-        const int vst = j % kPpStages;
+        const int vst = j % kPpVStages;
         const bool more = j + 1 < ntiles;
-        const int kst = (j + 1) % kPpStages;
-        mbar_wait(&bars->v_full[vst], (j / kPpStages) & 1);
+        const int kst = (j + 1) % kPpKStages;
+        mbar_wait(&bars->v_full[vst], (j / kPpVStages) & 1);
         for (int t = 0; t < 2; ++t) {
           mbar_wait(&bars->p_full[t], j & 1);
           mbar_wait(&bars->o_ready[t][j & 1], (j >> 1) & 1);
@@ -768,7 +816,7 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
           if (t == 1) umma_commit(&bars->v_empty[vst]);
           umma_commit(more ? &bars->corr_go[t][(j + 1) & 1] : &bars->o_final[t]);
           if (more) {
-            if (t == 0) mbar_wait(&bars->k_full[kst], ((j + 1) / kPpStages) & 1);
+            if (t == 0) mbar_wait(&bars->k_full[kst], ((j + 1) / kPpKStages) & 1);
             if (cta_aborted()) break;
             tc_fence_after();
             issue_s(t, kst);
@@ -794,50 +842,67 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
       const int n_valid = min(kTok, s_end - (s_begin + j * kTok));
       mbar_wait(&bars->s_full[t], j & 1);
       tc_fence_after();
-      // pass 1: the tile's row max, 64 columns per TMEM round trip
-      float mx = -INFINITY;
+      // pass 1: the tile's row max, 64 columns per TMEM round trip; four
+      // independent three-input max chains. Columns past the split's end
+      // (only in its last tile) read as -inf.
+      const bool full = n_valid == kTok;
+      float mx;
+      {
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sa[32], sb[32];
-        tmem_ld_32x32b_x32(scol + h * 64, sa);
-        tmem_ld_32x32b_x32(scol + h * 64 + 32, sb);
-        tmem_wait_ld();
+        for (int h = 0; h < 2; ++h) {
+          uint32_t sa[32], sb[32];
+          tmem_ld_32x32b_x32(scol + h * 64, sa);
+          tmem_ld_32x32b_x32(scol + h * 64 + 32, sb);
+          tmem_wait_ld();
+          if (!full) mask_cols(sa, sb, n_valid - h * 64);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if (h * 64 + e < n_valid) mx = fmaxf(mx, __uint_as_float(sa[e]));
-          if (h * 64 + 32 + e < n_valid) mx = fmaxf(mx, __uint_as_float(sb[e]));
+          for (int e = 0; e < 32; e += 4) {
+            m0 = fmax3f(m0, __uint_as_float(sa[e]), __uint_as_float(sa[e + 1]));
+            m1 = fmax3f(m1, __uint_as_float(sa[e + 2]), __uint_as_float(sa[e + 3]));
+            m2 = fmax3f(m2, __uint_as_float(sb[e]), __uint_as_float(sb[e + 1]));
+            m3 = fmax3f(m3, __uint_as_float(sb[e + 2]), __uint_as_float(sb[e + 3]));
+          }
         }
+        mx = fmax3f(m0, m1, fmaxf(m2, m3));
       }
       const float m_new = fmaxf(m, mx * sl2);
       const float dm = (m == -INFINITY) ? 1.f : ex2(m - m_new);
-      dmbuf[(t * 2 + (j & 1)) * kRows + r] = dm;
+      dmbuf[t * kRows + r] = dm;
       mbar_arrive(&bars->corr_go[t][j & 1]);
       // pass 2: P = round16(exp(S - m)) over the first 64 columns, row sum of
-      // the unrounded exps; 64 columns per round trip (P of columns
-      // [64h, 64h + 64) goes to [32h, 32h + 32): never over an S column a later
-      // load still reads)
-      float rs = 0.f;
+      // the unrounded exps (two packed accumulators); 64 columns per round
+      // trip (P of columns [64h, 64h + 64) goes to [32h, 32h + 32): never over
+      // an S column a later load still reads). A masked column gives
+      // exp2(-inf) = 0.
+      float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+      const float neg_m = -m_new;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         uint32_t sa[32], sb[32];
         tmem_ld_32x32b_x32(scol + h * 64, sa);
         tmem_ld_32x32b_x32(scol + h * 64 + 32, sb);
         tmem_wait_ld();
+        if (!full) mask_cols(sa, sb, n_valid - h * 64);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const uint32_t(&sv)[32] = q ? sb : sa;
           uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int c0 = h * 64 + q * 32 + e;
-            const float x0 = c0 < n_valid ? ex2(fmaf(__uint_as_float(sv[e]), sl2, -m_new)) : 0.f;
-            const float x1 = c0 + 1 < n_valid ? ex2(fmaf(__uint_as_float(sv[e + 1]), sl2, -m_new)) : 0.f;
-            rs += x0 + x1;
+          for (int e = 0; e < 32; e += 4) {
+            float y0, y1, y2, y3;
+            ffma2_bcast(y0, y1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), sl2, neg_m);
+            ffma2_bcast(y2, y3, __uint_as_float(sv[e + 2]), __uint_as_float(sv[e + 3]), sl2, neg_m);
+            const float x0 = ex2(y0), x1 = ex2(y1), x2 = ex2(y2), x3 = ex2(y3);
+            fadd2(r0, r1, x0, x1);
+            fadd2(r2, r3, x2, x3);
             pk[e >> 1] = pack2<kFp16>(x0, x1);
+            pk[(e >> 1) + 1] = pack2<kFp16>(x2, x3);
           }
           tmem_st_32x32b_x16(scol + h * 32 + q * 16, pk);
         }
       }
+      const float rs = (r0 + r1) + (r2 + r3);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->p_full[t]);
@@ -904,7 +969,7 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         mbar_wait(&bars->corr_go[t][j & 1], (j >> 1) & 1);
-        const float dm = dmbuf[(t * 2 + (j & 1)) * kRows + r];
+        const float dm = dmbuf[t * kRows + r];
         if (j >= 1 && __any_sync(0xffffffffu, dm != 1.f)) {
           tc_fence_after();
 #pragma unroll
@@ -931,16 +996,62 @@ __device__ __forceinline__ void paged_prefix_pp_body(const PagedAttnLaunch& p) {
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 14) {
-    tc_fence_after();
-    tmem_dealloc(tbase, kTmemCols);
-  }
+  return true;
 }
 
 template <bool kFp16>
 __global__ void __launch_bounds__(kPpThreads, 1) paged_prefix_pp_kernel(const __grid_constant__ PagedAttnLaunch p) {
   pdl_launch_dependents();
-  paged_prefix_pp_body<kFp16>(p);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PpBars* bars = reinterpret_cast<PpBars*>(smem + kPpOffBars);
+  if (threadIdx.x == 0) cta_wait_init(static_cast<uint64_t>(p.wait_limit_us) * 1000);
+  if (threadIdx.x >> 5 == 14) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+  if (p.piece_ctas == 0) {
+    // split grid: (split, kv head x row-tile pair, request)
+    const int split = blockIdx.x;
+    paged_prefix_pp_piece<kFp16>(p, smem, tbase, blockIdx.z, blockIdx.y % p.kv_heads, blockIdx.y / p.kv_heads,
+                                 split, split * p.split_tokens, split * p.split_tokens + p.split_tokens, 0, false);
+  } else {
+    // equal runs of the concatenated units' tiles; a unit's pieces are
+    // numbered by the CTAs that hold them, starting at the CTA that holds the
+    // unit's first tile: cf(x) = the CTA whose run contains tile x, i.e. the
+    // largest c with floor(c T / G) <= x
+    const int64_t mtiles = (static_cast<int64_t>(p.max_q_seqlen) * p.group + kRows - 1) / kRows;
+    const int64_t pairs = (mtiles + 1) / 2;
+    const int64_t tc = p.piece_unit_tiles;
+    const int64_t G = gridDim.x;
+    const int64_t T = static_cast<int64_t>(p.batch) * p.kv_heads * pairs * tc;
+    const int64_t c = blockIdx.x;
+    const int64_t hi = (c + 1) * T / G;
+    bool live = false;
+    for (int64_t x = c * T / G; x < hi;) {
+      const int64_t u = x / tc;
+      const int64_t ue = (u + 1) * tc;
+      const int64_t end = min(hi, ue);
+      const int64_t cf = ((u * tc + 1) * G + T - 1) / T - 1;
+      const int64_t b = u / (p.kv_heads * pairs), rem = u % (p.kv_heads * pairs);
+      live = paged_prefix_pp_piece<kFp16>(p, smem, tbase, static_cast<int>(b), static_cast<int>(rem / pairs),
+                                          static_cast<int>(rem % pairs), static_cast<int>(c - cf),
+                                          static_cast<int>((x - u * tc) * kTok), static_cast<int>((end - u * tc) * kTok),
+                                          end == ue ? p.num_splits : 0, live);
+      x = end;
+      if (cta_aborted()) break;  // read after the piece's CTA barrier: the same in every thread
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x >> 5 == 14) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
   if (p.pdl && threadIdx.x == 0) pdl_wait();
 }
 
@@ -950,7 +1061,7 @@ cudaError_t launch_paged_prefix_tc(const PagedAttnLaunch& p, bool fp16, cudaStre
   const int mtiles = (p.max_q_seqlen * p.group + kRows - 1) / kRows;
   if (mtiles >= 2 && (p.num_splits > 1 || p.partial_out || p.out_dtype == 2)) {
     // two row tiles per CTA (fp32 output or split partials)
-    dim3 grid(p.num_splits, p.kv_heads * ((mtiles + 1) / 2), p.batch);
+    const dim3 grid = p.piece_ctas ? dim3(p.piece_ctas) : dim3(p.num_splits, p.kv_heads * ((mtiles + 1) / 2), p.batch);
     auto kern = fp16 ? paged_prefix_pp_kernel<true> : paged_prefix_pp_kernel<false>;
     cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kPpSmemBytes);
     if (e != cudaSuccess) return e;
