@@ -101,21 +101,23 @@ def kernel_structure(q_len, group, kv_cap_tokens, T, H, KVH, batch, block_cols, 
 def stage1_pieces(q_len, group, KVH, batch, cap_tokens, sms=148, min_run=8):
     """The equal-run schedule of the two-tile stage-1 (pp_pieces in capi.cu):
     None when the split grid is used, else a function (b, g, mp) -> list of
-    (first tile, end tile) pieces of that unit, in 128-token KV tiles."""
+    (first tile, end tile) pieces of that unit, in 128-token KV tiles. Runs
+    cut the concatenated (request, kv head) streams; every row-tile pair of a
+    stream has the same pieces."""
     rows = q_len * group
     if q_len <= 0 or rows <= 128:
         return None
     pairs = -(-rows // 256)
-    units = KVH * batch * pairs
+    streams = KVH * batch
     tc = -(-max(1, cap_tokens) // 128)
-    T = units * tc
-    G = min(sms, T)
-    if G <= units or T < G * min_run:
+    T = streams * tc
+    G = min(sms // pairs, T)
+    if G <= streams or T < G * min_run:
         return None
-    starts = sorted(set([c * T // G for c in range(G)] + [T]))
+    starts = sorted(set([r * T // G for r in range(G)] + [T]))
 
     def pieces(b, g, mp):
-        u = (b * KVH + g) * pairs + mp
+        u = b * KVH + g
         lo, hi = u * tc, (u + 1) * tc
         cuts = [lo] + [x for x in starts if lo < x < hi] + [hi]
         return [(a - lo, e - lo) for a, e in zip(cuts[:-1], cuts[1:])]

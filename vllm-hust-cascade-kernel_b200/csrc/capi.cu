@@ -80,30 +80,33 @@ bool decode_planned(const cascade_paged_attn_t* p) {
 }
 
 // Equal-run schedule of the two-tile stage-1 (uniform q only): the 128-token
-// KV tiles of all (request, kv head, row-tile pair) units, concatenated, are
-// cut into one equal run per SM, so every CTA does the same number of tiles
-// whatever the unit count (C4: 64 units x 128 tiles; the split grid ran 128
-// CTAs of 64 tiles each and left 20 SMs idle). A run may end in one unit and
-// start the next; a unit's pieces go to consecutive partial planes. Used when
-// a run is shorter than a unit and at least kMinRunTiles long (the CTA's
-// pipeline refills at each piece boundary).
+// KV tiles of all (request, kv head) streams, concatenated, are cut into
+// equal runs, one per group of `pairs` CTAs (one CTA per row-tile pair of
+// the stream, so the pairs that read the same K/V tiles stay in lock step),
+// as many groups as fill the SMs once: every CTA does the same number of
+// tiles whatever the stream count (the split grid can leave SMs idle: C4 ran
+// 128 CTAs on 148 SMs). A run may end in one stream and start the next; a
+// stream's pieces go to consecutive partial planes. Used when a run is
+// shorter than a stream and at least kMinRunTiles long (the CTA's pipeline
+// refills at each piece boundary). *ctas = runs x pairs.
 constexpr int64_t kMinRunTiles = 8;
 bool pp_pieces(const cascade_paged_attn_t* p, int64_t* ctas, int64_t* unit_tiles, int64_t* planes) {
   if (p->q_seqlen_value <= 0) return false;
   const int64_t rows = p->q_seqlen_value * (p->num_heads / p->kv_heads);
   if (rows <= 128) return false;
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
-  const int64_t units = p->kv_heads * p->batch * ceil_div(rows, 256);
+  const int64_t pairs = ceil_div(rows, 256);
+  const int64_t streams = p->kv_heads * p->batch;
   const int64_t tc = ceil_div(cap, kTcTile);
-  const int64_t T = units * tc;
-  const int64_t G = std::min<int64_t>(kNumSMs, T);
-  if (G <= units || T < G * kMinRunTiles) return false;
-  // the CTA whose run [floor(c T / G), floor((c + 1) T / G)) holds tile x
-  auto cta_of = [&](int64_t x) { return ((x + 1) * G + T - 1) / T - 1; };
+  const int64_t T = streams * tc;
+  const int64_t G = std::min<int64_t>(kNumSMs / pairs, T);
+  if (G <= streams || T < G * kMinRunTiles) return false;
+  // the run [floor(r T / G), floor((r + 1) T / G)) that holds tile x
+  auto run_of = [&](int64_t x) { return ((x + 1) * G + T - 1) / T - 1; };
   int64_t most = 1;
-  for (int64_t u = 0; u < units; ++u) most = std::max(most, cta_of(u * tc + tc - 1) - cta_of(u * tc) + 1);
+  for (int64_t u = 0; u < streams; ++u) most = std::max(most, run_of(u * tc + tc - 1) - run_of(u * tc) + 1);
   if (most > kMaxSplits) return false;
-  *ctas = G;
+  *ctas = G * pairs;
   *unit_tiles = tc;
   *planes = most;
   return true;
@@ -127,9 +130,8 @@ void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens
     int64_t G, tc, planes;
     if (pp_pieces(p, &G, &tc, &planes)) {
       // equal runs: the longest piece, and one partial plane per piece of a unit
-      *split_tokens = ceil_div(tc * p->kv_heads * p->batch *
-                                   ceil_div(p->q_seqlen_value * (p->num_heads / p->kv_heads), 256),
-                               G) * kTcTile;
+      const int64_t pairs = ceil_div(p->q_seqlen_value * (p->num_heads / p->kv_heads), 256);
+      *split_tokens = ceil_div(tc * p->kv_heads * p->batch, G / pairs) * kTcTile;
       *num_splits = planes;
       return;
     }

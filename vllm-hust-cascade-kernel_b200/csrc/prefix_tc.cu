@@ -1020,26 +1020,28 @@ __global__ void __launch_bounds__(kPpThreads, 1) paged_prefix_pp_kernel(const __
     paged_prefix_pp_piece<kFp16>(p, smem, tbase, blockIdx.z, blockIdx.y % p.kv_heads, blockIdx.y / p.kv_heads,
                                  split, split * p.split_tokens, split * p.split_tokens + p.split_tokens, 0, false);
   } else {
-    // equal runs of the concatenated units' tiles; a unit's pieces are
-    // numbered by the CTAs that hold them, starting at the CTA that holds the
-    // unit's first tile: cf(x) = the CTA whose run contains tile x, i.e. the
-    // largest c with floor(c T / G) <= x
+    // equal runs of the concatenated (request, kv head) KV streams' tiles, each
+    // run taken by `pairs` adjacent CTAs (one per row-tile pair of the
+    // stream), so the pairs that read the same K/V tiles run in lock step and
+    // share them through L2. A stream's pieces are numbered by the runs that
+    // hold them, starting at the run that holds its first tile: cf(x) = the
+    // run containing tile x, the largest r with floor(r T / G) <= x
     const int64_t mtiles = (static_cast<int64_t>(p.max_q_seqlen) * p.group + kRows - 1) / kRows;
     const int64_t pairs = (mtiles + 1) / 2;
     const int64_t tc = p.piece_unit_tiles;
-    const int64_t G = gridDim.x;
-    const int64_t T = static_cast<int64_t>(p.batch) * p.kv_heads * pairs * tc;
-    const int64_t c = blockIdx.x;
-    const int64_t hi = (c + 1) * T / G;
+    const int64_t G = gridDim.x / pairs;
+    const int64_t T = static_cast<int64_t>(p.batch) * p.kv_heads * tc;
+    const int64_t run = blockIdx.x / pairs;
+    const int mp = static_cast<int>(blockIdx.x % pairs);
+    const int64_t hi = (run + 1) * T / G;
     bool live = false;
-    for (int64_t x = c * T / G; x < hi;) {
+    for (int64_t x = run * T / G; x < hi;) {
       const int64_t u = x / tc;
       const int64_t ue = (u + 1) * tc;
       const int64_t end = min(hi, ue);
       const int64_t cf = ((u * tc + 1) * G + T - 1) / T - 1;
-      const int64_t b = u / (p.kv_heads * pairs), rem = u % (p.kv_heads * pairs);
-      live = paged_prefix_pp_piece<kFp16>(p, smem, tbase, static_cast<int>(b), static_cast<int>(rem / pairs),
-                                          static_cast<int>(rem % pairs), static_cast<int>(c - cf),
+      live = paged_prefix_pp_piece<kFp16>(p, smem, tbase, static_cast<int>(u / p.kv_heads),
+                                          static_cast<int>(u % p.kv_heads), mp, static_cast<int>(run - cf),
                                           static_cast<int>((x - u * tc) * kTok), static_cast<int>((end - u * tc) * kTok),
                                           end == ue ? p.num_splits : 0, live);
       x = end;
