@@ -629,11 +629,12 @@ def read_roof_block(peaks, dom_gbs, reps=10, gib=2):
     best = max(v["gbs"] for v in res.values())
     del buf
     torch.cuda.empty_cache()
-    return {"what": "read-only streaming of a 2 GiB buffer (cascade_probe_hbm_read), 10 back-to-back launches "
-                    "per mode", "per_mode": res, "best_read_gbs": best,
-            "decode_kernel_frac_of_best_read": round(dom_gbs / best, 4),
-            "decode_kernel_frac_of_paged_pattern": round(dom_gbs / res["paged_tma_no_math"]["gbs"], 4),
-            "_launches": 4 * (reps + 2)}
+    out = {"what": "read-only streaming of a 2 GiB buffer (cascade_probe_hbm_read), 10 back-to-back launches "
+                   "per mode", "per_mode": res, "best_read_gbs": best, "_launches": 4 * (reps + 2)}
+    if dom_gbs is not None:
+        out["decode_kernel_frac_of_best_read"] = round(dom_gbs / best, 4)
+        out["decode_kernel_frac_of_paged_pattern"] = round(dom_gbs / res["paged_tma_no_math"]["gbs"], 4)
+    return out
 
 
 def host_wall_block(reps=300, seed=3):
@@ -878,6 +879,20 @@ def _jsonable(x):
     raise TypeError(f"not JSON serializable: {type(x).__name__}")
 
 
+def run_only(args):
+    """One block alone: the HBM read-roof probe, or stage-1 and the suffix
+    decode of C4 / C2 each timed alone (args.steps launches in one graph)."""
+    import torch
+    from cascade_kernel import workloads
+    torch.cuda.set_device(0)
+    if args.only == "read_roof":
+        return read_roof_block(_peaks(), None)
+    w = (workloads.c4_llama70b if args.only == "c4_kernels" else workloads.c2_llama8b)(seed=args.seed)
+    s1, dec = kernel_times(w, args.steps)
+    return {"block": args.only, "stage1_alone_us": round(s1, 2), "suffix_decode_alone_us": round(dec, 2),
+            "stage1_tflops": round(w.flops()["stage1"] / (s1 * 1e-6) / 1e12, 1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -891,7 +906,12 @@ def main():
                     help="skip the gate_up SwiGLU and add_rms_norm_stats sweeps")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the C4 sharded, C5 ragged, read-roof and host-wall blocks")
+    ap.add_argument("--only", choices=["read_roof", "c4_kernels", "c2_kernels"],
+                    help="run one block alone on cuda:0 and print its JSON (entry points for profiling)")
     args = ap.parse_args()
+    if args.only:
+        print(json.dumps(run_only(args), default=_jsonable), flush=True)
+        return
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
