@@ -122,6 +122,33 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def bind_to_gpu_numa(device):
+    """Restrict this process to the CPUs NVML reports as local to `device`
+    (read-only NVML query; nothing on the GPU changes), so the pinned host
+    buffers of the e2e copies, allocated afterwards, are placed on the GPU's
+    own NUMA node (first touch) instead of wherever the launcher started the
+    rank. Returns the CPU count bound to, or None when NVML is unavailable."""
+    try:
+        import pynvml
+        import torch
+        props = torch.cuda.get_device_properties(device)
+        pynvml.nvmlInit()
+        try:
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {w * 64 + b for w, m in enumerate(words) for b in range(64) if (int(m) >> b) & 1}
+        cpus &= set(range(os.cpu_count()))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+    except Exception:  # no NVML, an older driver, or a platform without affinity
+        return None
+    return None
+
+
 def setup_dist():
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -132,6 +159,7 @@ def setup_dist():
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.cuda.set_device(local)
+        bind_to_gpu_numa(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     else:
