@@ -1,8 +1,8 @@
 """Generate the committed golden fixtures from the reference's OWN golden code.
 
-Run in the build container, where the reference is mounted read-only:
+Run where a checkout of the reference is available (read-only is enough):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout> [stage1 merge norm precision]
 
 It imports, unmodified, the reference's CPU goldens
   * ascend-kernel/csrc/ops/fa_fp32_stage1/test/fa_fp32_ref.py
@@ -246,7 +246,9 @@ def make_norm(ref_dir, out_dir):
 
 
 def main():
-    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference checkout> [stage1 merge norm precision]")
+    ref_dir = sys.argv[1]
     out_dir = os.path.dirname(os.path.abspath(__file__))
     only = sys.argv[2:]  # optional subset: stage1 merge norm precision
     if not only or "stage1" in only:
