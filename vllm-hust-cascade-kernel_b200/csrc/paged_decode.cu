@@ -312,14 +312,17 @@ __device__ __forceinline__ void consume_tiles(const PagedAttnLaunch& p, uint8_t*
 }
 
 // Merge of the 4 consumer warps' (m, l, O) through shared memory at
-// merge_smem (kMergeBytes), then the item's output: a split partial (O, LSE)
-// or, for a single split, the final O and LSE.
+// merge_smem (merge_bytes(mrows): rows [0, mrows) of each warp, mrows >=
+// nrows), then the item's output: a split partial (O, LSE) or, for a single
+// split, the final O and LSE.
 constexpr int kSoStride = kHeadDim + 8;
-constexpr int kMergeBytes = (kConsumerWarps * 16 * kSoStride + 2 * kConsumerWarps * 16) * 4;
+__host__ __device__ constexpr int merge_bytes(int mrows) {
+  return (kConsumerWarps * mrows * kSoStride + 2 * kConsumerWarps * mrows) * 4;
+}
 template <bool kFp16>
-__device__ __forceinline__ void merge_store(const PagedAttnLaunch& p, float* merge_smem, const float (&o)[16][4],
-                                            float m0, float m1, float l0, float l1, int nrows, int tok0, int g,
-                                            int split) {
+__device__ __forceinline__ void merge_store(const PagedAttnLaunch& p, float* merge_smem, int mrows,
+                                            const float (&o)[16][4], float m0, float m1, float l0, float l1,
+                                            int nrows, int tok0, int g, int split) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gq = lane >> 2;
@@ -328,24 +331,28 @@ __device__ __forceinline__ void merge_store(const PagedAttnLaunch& p, float* mer
   // Rows are padded to 136 floats: the 8 rows of one fragment store then fall
   // on distinct banks (row r starts at bank 8r mod 32), and only the query
   // rows that exist are written.
-  float* so = merge_smem;                                      // [4][16][kSoStride]
-  float* sm = so + kConsumerWarps * 16 * kSoStride;           // [4][16]
-  float* sl = sm + kConsumerWarps * 16;                       // [4][16]
+  float* so = merge_smem;                                      // [4][mrows][kSoStride]
+  float* sm = so + kConsumerWarps * mrows * kSoStride;        // [4][mrows]
+  float* sl = sm + kConsumerWarps * mrows;                    // [4][mrows]
   if (gq < nrows) {
-    float* dst = so + (warp * 16 + gq) * kSoStride + 2 * tq;
+    float* dst = so + (warp * mrows + gq) * kSoStride + 2 * tq;
 #pragma unroll
     for (int n = 0; n < 16; ++n) *reinterpret_cast<float2*>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
   }
   if (gq + 8 < nrows) {
-    float* dst = so + (warp * 16 + gq + 8) * kSoStride + 2 * tq;
+    float* dst = so + (warp * mrows + gq + 8) * kSoStride + 2 * tq;
 #pragma unroll
     for (int n = 0; n < 16; ++n) *reinterpret_cast<float2*>(dst + n * 8) = make_float2(o[n][2], o[n][3]);
   }
   if (tq == 0) {
-    sm[warp * 16 + gq] = m0;
-    sm[warp * 16 + gq + 8] = m1;
-    sl[warp * 16 + gq] = l0;
-    sl[warp * 16 + gq + 8] = l1;
+    if (gq < nrows) {
+      sm[warp * mrows + gq] = m0;
+      sl[warp * mrows + gq] = l0;
+    }
+    if (gq + 8 < nrows) {
+      sm[warp * mrows + gq + 8] = m1;
+      sl[warp * mrows + gq + 8] = l1;
+    }
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
@@ -357,13 +364,13 @@ __device__ __forceinline__ void merge_store(const PagedAttnLaunch& p, float* mer
     const int d0 = (idx % (kHeadDim / 4)) * 4;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm[w * 16 + r]);
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm[w * mrows + r]);
     float wsum = 0.f, wt[kConsumerWarps];
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) {
-      const float mw = sm[w * 16 + r];
+      const float mw = sm[w * mrows + r];
       wt[w] = (mw == -INFINITY) ? 0.f : ex2(mw - M);
-      wsum += wt[w] * sl[w * 16 + r];
+      wsum += wt[w] * sl[w * mrows + r];
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
     const float lse_nat = (wsum > 0.f) ? (M + log2f(wsum)) * 0.6931471805599453f : -INFINITY;
@@ -373,7 +380,7 @@ __device__ __forceinline__ void merge_store(const PagedAttnLaunch& p, float* mer
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) {
       if (wt[w] == 0.f) continue;
-      const float4 v = *reinterpret_cast<const float4*>(&so[(w * 16 + r) * kSoStride + d0]);
+      const float4 v = *reinterpret_cast<const float4*>(&so[(w * mrows + r) * kSoStride + d0]);
       acc.x += wt[w] * v.x;
       acc.y += wt[w] * v.y;
       acc.z += wt[w] * v.z;
@@ -470,7 +477,7 @@ __device__ __forceinline__ int paged_decode_item(const PagedAttnLaunch& p, uint8
   // All tiles are consumed (every full barrier was waited by every warp), so
   // the stage ring is free for the merge once all consumer warps reach its
   // first barrier.
-  merge_store<kFp16>(p, reinterpret_cast<float*>(smem), o, m0, m1, l0, l1, nrows, tok0, g, split);
+  merge_store<kFp16>(p, reinterpret_cast<float*>(smem), 16, o, m0, m1, l0, l1, nrows, tok0, g, split);
   return ntiles;
 }
 __device__ __forceinline__ uint8_t* decode_smem() {
@@ -496,15 +503,15 @@ __global__ void __launch_bounds__(kThreads, 2) paged_decode_kernel(const __grid_
 //   warp 5 (fetcher) takes the items (per-kv-head counter) and prepares each
 //     in one of two shared-memory slots: the item code, its kv length, the
 //     split's block-table entries and the item's query rows;
-//   warp 4 (producer) streams each slot's tiles into a 2-stage ring whose
-//     positions continue across items;
+//   warp 4 (producer) streams each slot's tiles into an NS-stage ring whose
+//     positions continue across items (3 stages when the rows of an item are
+//     few enough for two CTAs per SM, else 2);
 //   warps 0-3 (consumers) take Q from the slot, consume the tiles and merge
 //     through their own shared-memory area.
 // The ring never drains between items and no role waits on a global load
 // at an item boundary: the next item's metadata and rows arrive while the
 // current one streams. A slot is free again once the producer has issued its
 // tiles and every consumer warp has read its Q. Two CTAs per SM.
-constexpr int kSStages = 2;
 constexpr int kStreamThreads = kThreads + 32;
 
 struct __align__(16) StreamSlot {
@@ -512,35 +519,41 @@ struct __align__(16) StreamSlot {
   int32_t kv;
   int32_t pad[2];
   int32_t bt[kBtCache];
-  uint16_t q[16 * kHeadDim];  // the item's <= 16 query rows
 };
 
 struct __align__(16) StreamBarriers {
-  uint64_t full[kSStages];
-  uint64_t empty[kSStages];
+  uint64_t full[3];
+  uint64_t empty[3];
   uint64_t item_full[2];   // slot written (32 fetcher lanes)
   uint64_t item_empty[2];  // slot consumed (producer + one arrive per consumer warp)
   uint64_t stall;          // never completed: the debug_stall test hook waits on it
   int32_t code_bcast;      // the consumers' item code, read once and shared (named barrier 1)
-  int32_t pad[3];
+  int32_t pad[1];
   StreamSlot slot[2];
 };
 
-constexpr int kStreamSmemBytes = kSStages * kStageBytes + kMergeBytes + 1024 /*align*/ +
-                                 static_cast<int>(sizeof(StreamBarriers));
+// Shared memory of the streaming form for items of `rows` query rows: the
+// NS-stage ring, the consumers' merge area (rows per warp = rows), the
+// barriers and slots, then each slot's query rows (rows x 256 bytes).
+__host__ __device__ constexpr int stream_smem_bytes(int ns, int rows) {
+  return ns * kStageBytes + merge_bytes(rows) + static_cast<int>(sizeof(StreamBarriers)) + 2 * rows * kHeadDim * 2 +
+         1024 /*align*/;
+}
 
-template <bool kFp16>
+template <bool kFp16, int NS>
 __global__ void __launch_bounds__(kStreamThreads, 2)
     paged_decode_stream_kernel(const __grid_constant__ PagedAttnLaunch p) {
   pdl_launch_dependents();
   uint8_t* smem = decode_smem();
-  float* merge_smem = reinterpret_cast<float*>(smem + kSStages * kStageBytes);
-  StreamBarriers* bars = reinterpret_cast<StreamBarriers*>(smem + kSStages * kStageBytes + kMergeBytes);
+  const int nrows = p.q_seqlen_value * p.group;
+  float* merge_smem = reinterpret_cast<float*>(smem + NS * kStageBytes);
+  StreamBarriers* bars = reinterpret_cast<StreamBarriers*>(smem + NS * kStageBytes + merge_bytes(nrows));
+  uint16_t* qrows = reinterpret_cast<uint16_t*>(bars + 1);  // [2 slots][nrows][128]
   const int g = blockIdx.y;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kSStages; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], kConsumerWarps);
     }
@@ -555,7 +568,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
   pdl_wait();  // the item list, its count and the zeroed counters are complete
   __syncthreads();
   const size_t plane = static_cast<size_t>(p.num_tokens) * p.num_heads;
-  const int nrows = p.q_seqlen_value * p.group;
   const int cap = p.block_cols * p.block_size;
   for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
     const int kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(cap)));
@@ -591,7 +603,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
         if (lane == 0) sl.kv = static_cast<int>(min(p.kv_seqlens[b], static_cast<int64_t>(cap)));
         // query rows: nrows x 256 bytes as 16-byte chunks over the warp
         const uint4* qsrc = static_cast<const uint4*>(p.query);
-        uint4* qdst = reinterpret_cast<uint4*>(sl.q);
+        uint4* qdst = reinterpret_cast<uint4*>(qrows + q * nrows * kHeadDim);
         for (int c = lane; c < nrows * (kHeadDim / 8); c += 32) {
           const int r = c / (kHeadDim / 8), w = c % (kHeadDim / 8);
           const int t = b * p.q_seqlen_value + r / p.group, h = g * p.group + r % p.group;
@@ -619,14 +631,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       const int kv = sl.kv;
       const int s_end = min(kv, s_begin + p.split_tokens);
       const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
-      int issued = produce_tiles<kSStages, true>(p, smem, bars->full, bars->empty, sl.bt, b, g, s_begin, s_end, kv,
-                                                 ntiles, it0, 0, 0);
+      int issued = produce_tiles<NS, true>(p, smem, bars->full, bars->empty, sl.bt, b, g, s_begin, s_end, kv, ntiles,
+                                           it0, 0, 0);
       issued = __shfl_sync(0xffffffffu, issued, 0);
       __syncwarp();  // lane 0 has issued every tile: the slot's entries are no longer read
       if (lane == 0) mbar_arrive(&bars->item_empty[q]);
       it0 += issued;
     }
-    if (lane == 0 && cta_aborted()) drain_ring<kSStages>(bars->full, 0, it0);
+    if (lane == 0 && cta_aborted()) drain_ring<NS>(bars->full, 0, it0);
   } else {
     // ----------------------------------------------------------- consumers
     for (int j = 0;; ++j) {
@@ -646,14 +658,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       const int ntiles = s_end > s_begin ? (s_end - s_begin + kTile - 1) / kTile : 0;
       const int tok0 = b * p.q_seqlen_value;
       uint32_t qa[8][4];
-      load_q_frags(p, sl.q, nrows, tok0, g, qa);
+      load_q_frags(p, qrows + q * nrows * kHeadDim, nrows, tok0, g, qa);
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->item_empty[q]);
       float o[16][4];
       float m0, m1, l0, l1;
-      consume_tiles<kFp16, kSStages>(p, smem, bars->full, bars->empty, &bars->stall, it0, ntiles, s_begin, s_end, qa, o,
-                                     m0, m1, l0, l1);
-      merge_store<kFp16>(p, merge_smem, o, m0, m1, l0, l1, nrows, tok0, g, split);
+      consume_tiles<kFp16, NS>(p, smem, bars->full, bars->empty, &bars->stall, it0, ntiles, s_begin, s_end, qa, o, m0,
+                               m1, l0, l1);
+      merge_store<kFp16>(p, merge_smem, nrows, o, m0, m1, l0, l1, nrows, tok0, g, split);
       it0 += ntiles;
     }
   }
@@ -759,11 +771,17 @@ cudaError_t launch_paged_decode(const PagedAttnLaunch& p, bool fp16, cudaStream_
     launch_maybe_pdl(decode_plan_kernel, dim3(1), dim3(1024), 0, stream, p.pdl != 0, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    auto kern = fp16 ? paged_decode_stream_kernel<true> : paged_decode_stream_kernel<false>;
-    e = ensure_smem_limit(reinterpret_cast<const void*>(kern), kStreamSmemBytes);
+    // three ring stages when two CTAs per SM still fit (up to 228 KB of
+    // shared memory per SM, 1 KB reserved per CTA), else two
+    const int rows = p.q_seqlen_value * p.group;
+    const bool three = 2 * (stream_smem_bytes(3, rows) + 1024) <= 228 * 1024;
+    const int smem = stream_smem_bytes(three ? 3 : 2, rows);
+    auto kern = three ? (fp16 ? paged_decode_stream_kernel<true, 3> : paged_decode_stream_kernel<false, 3>)
+                      : (fp16 ? paged_decode_stream_kernel<true, 2> : paged_decode_stream_kernel<false, 2>);
+    e = ensure_smem_limit(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
     const int per_head = std::max(1, (2 * kNumSMs) / std::max(1, p.kv_heads));
-    return launch_maybe_pdl(kern, dim3(per_head, p.kv_heads, 1), dim3(kStreamThreads), kStreamSmemBytes, stream, true,
+    return launch_maybe_pdl(kern, dim3(per_head, p.kv_heads, 1), dim3(kStreamThreads), smem, stream, true,
                             p);
   }
   dim3 grid(p.num_splits, p.kv_heads, p.batch);
