@@ -67,6 +67,61 @@ def test_fused_step_and_chain_vs_oracle(name):
         assert (err <= O.ulp(ref, dt) + 2e-3).all(), float((err - O.ulp(ref, dt)).max())
 
 
+def _combine_case(form):
+    """Step shapes of 2,560 (token, head) rows -- more than one wave of the
+    two-blocks-per-SM combine grid -- whose plans (stage-1 planes n1, suffix
+    splits n2) select each of the step combine's other forms: n1 + n2 = 3
+    (4-deep dense), 6 (8-deep dense) and 16 (sparse: one 6,000-token suffix
+    makes 12 splits that most rows leave empty; some suffixes are empty)."""
+    rng = np.random.default_rng(11)
+    if form == "dense4":
+        return dict(group_sizes=[80], prefix_lens=[256], suffix_lens=list(rng.integers(1, 400, 80)), H=32, KVH=8,
+                    bs=64, dtype="bf16", seed=5), 3
+    if form == "dense8":
+        return dict(group_sizes=[40, 40], prefix_lens=[1024, 600], suffix_lens=list(rng.integers(1, 2000, 80)),
+                    H=32, KVH=8, bs=64, dtype="bf16", seed=6), 6
+    suf = list(rng.integers(0, 300, 80))
+    suf[7] = 6000
+    return dict(group_sizes=[20] * 4, prefix_lens=[100, 2000, 37, 640], suffix_lens=suf, H=32, KVH=8, bs=16,
+                dtype="fp16", seed=7), 16
+
+
+@pytest.mark.parametrize("form", ["dense4", "dense8", "sparse"])
+def test_step_combine_forms_vs_oracle(form):
+    import torch
+    from cascade_kernel import capi
+    from cascade_kernel.cascade import cascade_decode
+    Hh.need_cuda()
+    kw, n_planes = _combine_case(form)
+    dt = kw["dtype"]
+    kw["dtype"] = torch.float16 if dt == "fp16" else torch.bfloat16
+    w = _work(form, **kw)
+    t = w.tables
+    # the planes the step merges: stage-1's plan (prefix-first: at most 32
+    # CTAs over the (kv head, row-tile pair) units) and the suffix splits
+    dp = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens,
+                         t.uniform_group)
+    ds = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens, t.suffix_kv_seqlens, 1)
+    pa, pb = capi.plan(dp, t.uniform_group, False), capi.plan(ds, 1, True)
+    cdiv = lambda a, b: -(-a // b)
+    rows_pf = t.uniform_group * (kw["H"] // kw["KVH"])
+    units = kw["KVH"] * len(kw["group_sizes"]) * cdiv(rows_pf, 256 if rows_pf > 128 else 128)
+    n1 = pa.num_splits
+    if pa.kernel == 1 and units <= 24:
+        cap = dp.block_cols * dp.block_size
+        split_tokens = cdiv(cdiv(cap, min(cdiv(32, units), cdiv(cap, 128))), 128) * 128
+        n1 = cdiv(cap, split_tokens)
+    assert w.q.shape[0] * w.q.shape[1] == 2560 and n1 + pb.num_splits == n_planes
+    got = cascade_decode(w.q, w.k_pool, w.v_pool, w.tables, fused=True)
+    torch.cuda.synchronize()
+    assert Hh.capi().device_error() == 0
+    ref, _ = _oracle(w, round_suffix=False, out_dtype="fp32")
+    got = Hh.dev_to_f64(got)
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref)
+    assert (err <= O.ulp(ref, dt) + 2e-3).all(), float((err - O.ulp(ref, dt)).max())
+
+
 def test_fused_equals_chain_at_benchmark_shape():
     """C2 (B=64, prefix 4096, suffix U[128,1024], 32/8 heads): the fused step and
     the three-op chain differ by the chain's rounding of the suffix partial to

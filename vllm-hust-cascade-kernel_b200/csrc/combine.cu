@@ -7,8 +7,21 @@
 // Partials with lse = -inf (empty splits, zero-length suffixes) get weight 0.
 //
 // One warp per row: lane i reads lse_i, the weights come from warp
-// reductions, each lane then owns 4 of the 128 dims and issues the partial
-// loads (16 B each) for every non-empty split.
+// reductions, each lane then owns 4 of the 128 dims. The kernel is
+// latency-bound (a round of dependent loads per row), so its form follows
+// the step's shape (n = n1 + n2 planes):
+//  * dense (kPre = 4, 8 or 16 >= n): every partial is loaded before the
+//    weights are known, one round per row. Grids of at most two blocks per
+//    SM take the 16-deep form, whose 93 registers keep two blocks per SM and
+//    so spread the rows over the most SMs (C2: 2,048 rows, 35.6 us step
+//    against 36.4 with the 55-register form, whose blocks land four or more
+//    to an SM); larger grids take the smallest depth that holds n, so no
+//    register waits for a load never issued and more rows are in flight;
+//  * sparse (kPre = 0, n > 8 on larger grids): ragged suffixes make many
+//    splits but leave most of a row's partials empty, so the weights come
+//    first and only the partials with a non-zero weight are loaded, eight
+//    per round (C5 step 297-307 -> 278-284 us; C4, 8 planes on 16,384 rows,
+//    372.7 -> 369.1 us).
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -17,16 +30,17 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(const CascadeCombineLaunch p) {
+template <int kPre>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, kPre == 4 ? 6 : kPre == 16 ? 2 : 4)
+    cascade_combine_kernel(const CascadeCombineLaunch p) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (p.pdl) pdl_wait();  // partials come from the kernels before this one
   if (row >= p.rows) return;
   const int n = p.n1 + p.n2;
-  // Every load of the row is issued before any result is needed: the lse of
-  // partial `lane` / `lane+32`, and this lane's 4 dims of the first 16
-  // partials. A partial with lse = -inf may hold anything: it is selected
-  // out, never multiplied.
+  // The lse of partial `lane` / `lane+32`, and (dense form) this lane's 4
+  // dims of every partial, all issued before any result is needed. A partial
+  // with lse = -inf may hold anything: it is selected out, never multiplied.
   auto part_ptr = [&](int i) -> const float4* {
     const float* base = i < p.n1 ? p.o1 + (static_cast<int64_t>(i) * p.rows + row) * kHeadDim
                                  : p.o2 + (static_cast<int64_t>(i - p.n1) * p.rows + row) * kHeadDim;
@@ -38,10 +52,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(co
     const int i = lane + 32;
     lb = i < p.n1 ? p.l1[i * p.rows + row] : p.l2[(i - p.n1) * p.rows + row];
   }
-  constexpr int kPre = 16;
-  float4 v[kPre];
+  constexpr int kHeld = kPre > 0 ? kPre : 1;
+  float4 v[kHeld];
+  if constexpr (kPre > 0) {
 #pragma unroll
-  for (int k = 0; k < kPre; ++k) v[k] = k < n ? __ldg(part_ptr(k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < kPre; ++k) v[k] = k < n ? __ldg(part_ptr(k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float m = fmaxf(la, lb);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -59,11 +75,32 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(co
       acc.w += w * x.w;
     }
   };
+  if constexpr (kPre > 0) {
 #pragma unroll
-  for (int k = 0; k < kPre; ++k) add(__shfl_sync(0xffffffffu, wa, k), v[k]);
-  for (int i = kPre; i < n; ++i) {  // rare: more than 16 partials per row
-    const float w = __shfl_sync(0xffffffffu, i < 32 ? wa : wb, i & 31);
-    if (w != 0.f) add(w, __ldg(part_ptr(i)));
+    for (int k = 0; k < kPre; ++k) add(__shfl_sync(0xffffffffu, wa, k), v[k]);
+  } else {
+    // Partials with a non-zero weight, as a warp-uniform bit set over the
+    // (at most 64) planes; eight of them loaded per round.
+    uint64_t live = static_cast<uint64_t>(__ballot_sync(0xffffffffu, wa != 0.f)) |
+                    (static_cast<uint64_t>(__ballot_sync(0xffffffffu, wb != 0.f)) << 32);
+    constexpr int kBatch = 8;
+    while (live != 0) {
+      float4 x[kBatch];
+      float w[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        w[k] = 0.f;
+        x[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live != 0) {
+          const int i = __ffsll(static_cast<long long>(live)) - 1;
+          live &= live - 1;
+          w[k] = __shfl_sync(0xffffffffu, i < 32 ? wa : wb, i & 31);
+          x[k] = __ldg(part_ptr(i));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) add(w[k], x[k]);
+    }
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   const int64_t o = row * kHeadDim + lane * 4;
@@ -84,7 +121,13 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cascade_combine_kernel(co
 cudaError_t launch_cascade_combine(const CascadeCombineLaunch& p, cudaStream_t stream) {
   if (p.rows == 0) return cudaSuccess;
   const unsigned blocks = static_cast<unsigned>((p.rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
-  return launch_maybe_pdl(cascade_combine_kernel, dim3(blocks), dim3(kWarpsPerBlock * 32), 0, stream, p.pdl != 0, p);
+  const int n = p.n1 + p.n2;
+  const bool one_wave = blocks <= 2u * kNumSMs;
+  auto kern = one_wave && n <= 16 ? cascade_combine_kernel<16>
+              : n <= 4            ? cascade_combine_kernel<4>
+              : n <= 8            ? cascade_combine_kernel<8>
+                                  : cascade_combine_kernel<0>;
+  return launch_maybe_pdl(kern, dim3(blocks), dim3(kWarpsPerBlock * 32), 0, stream, p.pdl != 0, p);
 }
 
 }  // namespace cascade
