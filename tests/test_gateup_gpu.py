@@ -138,12 +138,15 @@ def test_swiglu_llama8b_shapes_vs_torch_fp32(M):
 
 
 @pytest.mark.parametrize("M,K,I", [(200, 4096, 14336), (256, 8192, 3584), (129, 1024, 640), (256, 64, 128),
-                                   (256, 256, 20480), (136, 208, 20480), (256, 128, 17024)])
+                                   (256, 256, 20480), (136, 208, 20480), (256, 128, 17024), (256, 8192, 7168),
+                                   (136, 1040, 512), (200, 512, 1792)])
 def test_swiglu_256_row_forms(M, K, I):
     """129..256 rows (the CTA-pair 256 x 256 or 256 x 224 tile, the one-CTA
     256-row tile with a shared W tile, or the 128-row forms the launcher picks
-    by tile count; 80 / 76 pair tiles for more tiles than pairs), K from one
-    block to 8192 and a ragged last K block:
+    by tile count; 80 / 76 pair tiles for more tiles than pairs; the split-K
+    cluster of pairs for narrow shards: 4 splits at I = 3584 and 512 -- the
+    latter with a ragged last K block and 17 K blocks split 4/4/4/5 -- and 2
+    at I = 7168 and 1792), K from one block to 8192 and a ragged last K block:
     within one bf16 ulp of torch fp32 (+ GEMM order noise), bit-identical on
     a second call, no device error, and the C ABI equal to the op."""
     import torch

@@ -575,6 +575,292 @@ cudaError_t launch_pair(const GateUpLaunch& L, const void* a, const void* b, cud
 }
 
 // ---------------------------------------------------------------------------
+// Split-K CTA-pair form for SwiGLU over 129..256 rows on narrow shards (few
+// 256-column pair tiles: a Llama-3-70B MLP shard over 4 or 8 GPUs has
+// I = 7168 / 3584, 28 / 14 tiles). The pair tile already fills TMEM (512
+// accumulator columns per CTA), so more tiles per SM would move more operand
+// bytes through L2 per FLOP; splitting K instead puts more SMs on each tile at
+// the pair tile's traffic per FLOP. A cluster of 2S CTAs = S pairs computes
+// one 256 x 256 output tile: pair s (cluster ranks 2s, 2s+1; its leader 2s
+// issues the MMAs) accumulates K blocks [s*kb/S, (s+1)*kb/S) exactly as the
+// pair form does. The S partial accumulators are reduced through distributed
+// shared memory: output columns [s*W, (s+1)*W) of the tile (W = 256 / S)
+// belong to pair s; each CTA of another pair reads the gate and up columns of
+// that range for its 128 rows from TMEM and stores them into the owner's
+// operand ring, free once every pair's MMAs are done (one [128 x 2W] fp32
+// slot per sender, in 16-column blocks; each warp transposes its rows through
+// a small local buffer so that every remote store instruction writes 512
+// contiguous bytes); the owner adds its own columns and the slots in a
+// fixed order (its own, then the senders by split index: the result does not
+// depend on timing), applies SwiGLU and TMA-stores its [128 x W] bf16 block.
+// No global scratch: mode 1 keeps its workspace-free contract. Three cluster
+// barriers, taken by every thread of every CTA on every path (an aborted CTA
+// included), order the exchange: rings free / slots written / TMEM and peer
+// stores done before teardown.
+// ---------------------------------------------------------------------------
+template <int S>
+struct SplitCfg {
+  static_assert(S == 2 || S == 4, "K splits per cluster: 2 or 4 (clusters of 4 or 8 CTAs)");
+  static constexpr int C = 128;
+  static constexpr int W = 2 * C / S;               // output columns one pair reduces
+  static constexpr int kRingBytes = PairCfg<C>::kStagingOff;
+  // A receive slot holds one sender's gate | up columns of the owner's range
+  // for the 128 rows as 2W/16 blocks of [128 rows x 16 fp32] (8 KB each),
+  // the 16-byte chunk k of row r stored at chunk k ^ ((r >> 1) & 3): 8
+  // consecutive rows of one chunk fall in 8 different bank groups.
+  static constexpr int kBlocks = 2 * W / 16;
+  static constexpr int kSlotBytes = kBlocks * kBM * 64;
+  static constexpr int kSendOff = (S - 1) * kSlotBytes;  // per-warp [32 rows x 16 fp32] transpose buffers
+  static constexpr int kSendBytes = 4 * 32 * 64;
+  static constexpr int kStgOff = kSendOff + kSendBytes;
+  static constexpr int kStgBytes = kBM * W * 2;     // [128 x W] bf16 in 64-column SW128 boxes
+  static constexpr int kBarOff = (kStgOff + kStgBytes > kRingBytes ? kStgOff + kStgBytes : kRingBytes);
+  static constexpr int kSmem = kBarOff + 256 + 1024;
+  static_assert(kStgOff % 1024 == 0, "staging boxes start on a swizzle atom");
+  static_assert(kSmem <= 227 * 1024, "shared memory budget");
+};
+
+template <int S>
+__global__ void __launch_bounds__(kThreads, 1) gateup_pair_split_kernel(const __grid_constant__ GemmParams p) {
+  using Cfg = SplitCfg<S>;
+  using PC = PairCfg<128>;
+  constexpr int C = 128, W = Cfg::W;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + Cfg::kBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_cta_rank();
+  const uint32_t prank = crank & 1u, leader = crank & ~1u;  // role in the pair, the pair's MMA issuer
+  const int split = static_cast<int>(crank >> 1);
+  const int tile = static_cast<int>(blockIdx.x) / (2 * S);
+  const int kb0 = split * p.num_kb / S, kb1 = (split + 1) * p.num_kb / S;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << leader);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->drain, 1);
+    fence_mbar_init();
+    cta_wait_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // barriers and TMEM of every CTA are ready
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
+      const int wrow = (prank == 0 ? 0 : p.I) + tile * 2 * C;  // gate rows (even rank) or up rows (odd)
+      int it = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int st = it % kPairStages;
+        if (it >= kPairStages) mbar_wait_cluster(&bars->empty[st], ((it / kPairStages) - 1) & 1);
+        if (cta_aborted()) break;
+        const uint32_t full_l = mapa_shared(smem_u32(&bars->full[st]), leader);
+        if (prank == 0) mbar_arrive_expect_tx(&bars->full[st], 2 * PC::kStageBytes);
+        uint8_t* sa = smem + st * PC::kStageBytes;
+        uint8_t* sb = sa + PC::kABytes;
+        tma_load_2d_pair(sa, &p.tm_a, full_l, kb * kBK, static_cast<int>(prank) * kBM);
+        tma_load_2d_pair(sb, &p.tm_b, full_l, kb * kBK, wrow);
+        tma_load_2d_pair(sb + PC::kBHalf, &p.tm_b, full_l, kb * kBK, wrow + C);
+      }
+      if (cta_aborted()) {
+        if (prank == 0) {
+          for (int i = it > kPairStages ? it - kPairStages : 0; i < it; ++i)
+            mbar_wait_cluster_drain(&bars->full[i % kPairStages], (i / kPairStages) & 1);
+        } else {
+          // the odd CTA cannot observe the leader's barriers: give its own
+          // last loads time to land before teardown
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && prank == 0) {
+      const uint32_t idesc = make_idesc_f16(256, 2 * C, 1, 0, 0);
+      int it = 0;
+      tc_fence_after();
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int st = it % kPairStages;
+        mbar_wait_cluster(&bars->full[st], (it / kPairStages) & 1);
+        if (cta_aborted()) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + st * PC::kStageBytes);
+        const uint32_t b0 = a0 + PC::kABytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const uint64_t ad = make_smem_desc(a0 + k * 32, 16, 1024, 2);
+          const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+          umma_f16_ss_pair(tbase, ad, make_smem_desc(b0 + k * 32, 16, 1024, 2), idesc, acc);
+          umma_f16_ss_pair(tbase + 2 * C, ad, make_smem_desc(b0 + PC::kBHalf + k * 32, 16, 1024, 2), idesc, acc);
+        }
+        umma_commit_pair(&bars->empty[st], pair_mask);
+      }
+      umma_commit_pair(&bars->acc_full, pair_mask);
+      if (cta_aborted()) {
+        umma_commit_pair(&bars->drain, static_cast<uint16_t>(1u << leader));
+        mbar_wait_cluster_drain(&bars->drain, 0);
+      }
+    }
+  } else {
+    mbar_wait_cluster(&bars->acc_full, 0);  // this pair's partial sums are in TMEM
+  }
+
+  // ---- exchange: every CTA's ring is free once every pair's MMAs are done
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const int q = warp & 3;
+  const int r = q * 32 + lane;  // this thread's TMEM lane = row of the CTA's 128
+  const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+  // Row r's 16-byte chunk k within a [rows x 16 fp32] block (see SplitCfg).
+  const uint32_t row_chunk = static_cast<uint32_t>(r) * 64;
+  const uint32_t swz = static_cast<uint32_t>((r >> 1) & 3);
+  if (warp >= 2) {
+    // Each warp moves its 32 rows one 16-column block at a time: TMEM ->
+    // registers -> its transpose buffer (local, swizzled) -> 512 contiguous
+    // bytes per remote store instruction (a warp-wide store that scatters
+    // over 32 rows is about twice as slow through the cluster network).
+    uint8_t* xb = smem + Cfg::kSendOff + q * 2048;
+    const uint32_t xrow = static_cast<uint32_t>(lane) * 64;
+    for (int j = 0; j < S; ++j) {
+      if (j == split) continue;
+      const int slot = split < j ? split : split - 1;
+      const uint32_t dst = mapa_shared(smem_u32(smem + slot * Cfg::kSlotBytes + q * 2048 + lane * 16),
+                                       static_cast<uint32_t>(2 * j) + prank);
+      const int col0 = j * W;
+      const uint32_t gsrc = tbase + lane_off + (col0 / C) * 2 * C + (col0 % C);
+#pragma unroll 1
+      for (int b = 0; b < Cfg::kBlocks; ++b) {
+        // blocks [0, W/16): gate columns; [W/16, 2W/16): the same up columns
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(gsrc + (b < W / 16 ? b * 16 : C + (b - W / 16) * 16), v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<uint4*>(xb + xrow + ((k ^ swz) << 4)) = make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 w4 = *reinterpret_cast<const uint4*>(xb + k * 512 + lane * 16);
+          st_cluster_v4(dst + b * (kBM * 64) + k * 512, w4.x, w4.y, w4.z, w4.w);
+        }
+        __syncwarp();
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // the slots are written (release / acquire)
+  tc_fence_after();
+  if (warp >= 2) {
+    const int etid = threadIdx.x - 64;
+    const int col0 = split * W;
+    const uint32_t gsrc = tbase + lane_off + (col0 / C) * 2 * C + (col0 % C);
+    uint8_t* stg = smem + Cfg::kStgOff;
+#pragma unroll 1
+    for (int c = 0; c < W / 16; ++c) {
+      uint32_t gr[16], ur[16];
+      tmem_ld_32x32b_x16(gsrc + c * 16, gr);
+      tmem_ld_32x32b_x16(gsrc + C + c * 16, ur);
+      tmem_wait_ld();
+      float g[16], u[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        g[e] = __uint_as_float(gr[e]);
+        u[e] = __uint_as_float(ur[e]);
+      }
+#pragma unroll
+      for (int s = 0; s < S - 1; ++s) {
+        const uint8_t* gb = smem + s * Cfg::kSlotBytes + c * (kBM * 64) + row_chunk;
+        const uint8_t* ub = gb + (W / 16) * (kBM * 64);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 gv = *reinterpret_cast<const float4*>(gb + ((k ^ swz) << 4));
+          const float4 uv = *reinterpret_cast<const float4*>(ub + ((k ^ swz) << 4));
+          const int e = 4 * k;
+          g[e] += gv.x, g[e + 1] += gv.y, g[e + 2] += gv.z, g[e + 3] += gv.w;
+          u[e] += uv.x, u[e + 1] += uv.y, u[e + 2] += uv.z, u[e + 3] += uv.w;
+        }
+      }
+      uint32_t pk[8];
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) pk[e >> 1] = pack2<false>(silu_mul(g[e], u[e]), silu_mul(g[e + 1], u[e + 1]));
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int ch = c * 2 + hh;  // 16-byte chunk of the row's W bf16
+        *reinterpret_cast<uint4*>(stg + (ch >> 3) * (kBM * 128) + sw128(r, ch & 7)) =
+            make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
+      }
+    }
+    fence_proxy_async_smem();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (etid == 0) {
+      const int n0 = tile * 2 * C + col0;
+#pragma unroll
+      for (int b = 0; b < W / 64; ++b) tma_store_2d(&p.tm_d, stg + b * (kBM * 128), n0 + b * 64, static_cast<int>(prank) * kBM);
+      bulk_commit_group();
+      bulk_wait_group0();
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // no CTA still reads TMEM or stores into a peer's shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 512);
+  }
+}
+
+template <int S>
+cudaError_t launch_pair_split(const GateUpLaunch& L, const void* a, const void* b, cudaStream_t stream) {
+  using Cfg = SplitCfg<S>;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = L.M;
+  p.K = L.K;
+  p.I = L.I;
+  p.num_m = 1;
+  p.num_n = L.I / 256;
+  p.num_kb = (L.K + kBK - 1) / kBK;
+  p.mode = L.mode;
+  if (!enc(&p.tm_a, a, L.K, L.M, static_cast<uint64_t>(L.K) * 2, kBM)) return cudaErrorInvalidValue;
+  if (!enc(&p.tm_b, b, L.K, 2ull * L.I, static_cast<uint64_t>(L.K) * 2, Cfg::C)) return cudaErrorInvalidValue;
+  if (!encode_tmap_2d(&p.tm_d, L.d, L.I, L.M, static_cast<uint64_t>(L.d_stride) * 2, 64, kBM, true,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+    return cudaErrorInvalidValue;
+  cudaError_t e = ensure_smem_limit(reinterpret_cast<const void*>(gateup_pair_split_kernel<S>), Cfg::kSmem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2 * S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * S * p.num_n);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gateup_pair_split_kernel<S>, p);
+}
+
+// ---------------------------------------------------------------------------
 // Small-M variant (M <= 128, the weight-streaming regime): swap the operands so
 // the paired weight tile fills the 128-row MMA side. D^T[128 x MP] =
 // W_tile[128 x K] X^T[K x MP], W_tile = gate rows [n0, n0+64) followed by the
@@ -766,6 +1052,16 @@ cudaError_t launch_gateup(const GateUpLaunch& L, const void* a, const void* b, c
   // halves (measured: equal at K=4096, 4% faster at K=8192); beyond, the
   // overlapped-epilogue form wins (684 vs 725 us at M=4096)
   if (L.M <= 2 * kBM) {
+    // Narrow SwiGLU shards: K split over a cluster of pairs when the pair
+    // tiles alone would leave most SMs idle and the split still fits one wave
+    // of clusters (16 clusters of 8 / 32 of 4 CTAs on 148 SMs), each split
+    // keeping at least 4 K blocks.
+    if (L.mode == 1 && L.M > kBM && L.I % 256 == 0) {
+      const int64_t pair_tiles = L.I / 256;
+      const int num_kb = (L.K + kBK - 1) / kBK;
+      if (pair_tiles * 8 <= 128 && num_kb >= 16) return launch_pair_split<4>(L, a, b, stream);
+      if (pair_tiles * 4 <= 128 && num_kb >= 8) return launch_pair_split<2>(L, a, b, stream);
+    }
     // Few rows: the weight stream is spread over as many CTAs as there are
     // SMs. Of the tile forms (256 x 128 with a shared W tile, 128 x 128,
     // 128 x 64), take the one with the most tiles that still fits in one
