@@ -339,6 +339,16 @@ def run_ours(args, rank, world, local):
     mlp70 = (gateup_sweep(flush, peaks, Ms=(256,), K=8192, I=28672 // world, seed=11 + rank)
              if not args.no_gateup and 28672 % (128 * world) == 0 else None)
 
+    # on one GPU, the same shard at the widths 2, 4 and 8 ranks own (the
+    # narrow ones take the split-K cluster-of-pairs form)
+    mlp70_widths = None
+    if not args.no_gateup and world == 1:
+        mlp70_widths = {"per_ranks": {}, "_launches": 0}
+        for r in (2, 4, 8):
+            blk = gateup_sweep(flush, peaks, Ms=(256,), K=8192, I=28672 // r, seed=11)
+            mlp70_widths["_launches"] += blk.pop("_launches")
+            mlp70_widths["per_ranks"][str(r)] = dict(blk["per_M"]["256"], I=28672 // r)
+
     norm = norm_sweep(flush, peaks) if not args.no_gateup else None
 
     verify = verify_sharded(args, rank, world, outs[0]) if world > 1 else None
@@ -415,6 +425,11 @@ def run_ours(args, rank, world, local):
                           f"silu(gate)*up bf16 [256,{28672 // world}] per rank ({world} rank(s))")
         line["gateup_swiglu_70b_shard"] = mlp70
         line["gpu_launches"] += mlp70.pop("_launches")
+    if mlp70_widths is not None:
+        line["gpu_launches"] += mlp70_widths.pop("_launches")
+        mlp70_widths["shape"] = ("Llama-3-70B MLP shard on one GPU at the per-rank width of 2/4/8 ranks: "
+                                 "X[256,8192] x W[2*28672/r,8192]^T -> silu(gate)*up bf16 [256,28672/r]")
+        line["gateup_swiglu_70b_shard_widths"] = mlp70_widths
     if norm is not None:
         line["add_rms_norm_stats"] = norm
         line["gpu_launches"] += norm.pop("_launches")
@@ -908,13 +923,27 @@ def _jsonable(x):
 
 
 def run_only(args):
-    """One block alone: the HBM read-roof probe, or stage-1 and the suffix
-    decode of C4 / C2 each timed alone (args.steps launches in one graph)."""
+    """One block alone: the HBM read-roof probe; stage-1 and the suffix
+    decode of C4 / C2 each timed alone (args.steps launches in one graph); the
+    whole C4 step (args.steps steps in one graph); or the Llama-3-70B MLP
+    gate_up shard at the per-rank width of args.shard_ranks ranks (args.steps
+    event-timed calls)."""
     import torch
     from cascade_kernel import workloads
     torch.cuda.set_device(0)
     if args.only == "read_roof":
         return read_roof_block(_peaks(), None)
+    if args.only == "gateup_70b_shard":
+        I = 28672 // args.shard_ranks
+        blk = gateup_sweep(lambda: None, _peaks(), Ms=(256,), K=8192, I=I, reps=args.steps, seed=11)
+        return {"block": args.only, "ranks": args.shard_ranks, "I": I, **blk["per_M"]["256"]}
+    if args.only == "c4_step":
+        from cascade_kernel.cascade import CascadeStepGraph
+        w = workloads.c4_llama70b(seed=args.seed)
+        g = CascadeStepGraph(w.q, w.k_pool, w.v_pool, w.tables)
+        for _ in range(3):
+            g.replay()
+        return {"block": args.only, "us_per_step": round(_time_graph(g, args.steps, torch.cuda.current_stream()) * 1e3, 2)}
     w = (workloads.c4_llama70b if args.only == "c4_kernels" else workloads.c2_llama8b)(seed=args.seed)
     s1, dec = kernel_times(w, args.steps)
     return {"block": args.only, "stage1_alone_us": round(s1, 2), "suffix_decode_alone_us": round(dec, 2),
@@ -934,8 +963,10 @@ def main():
                     help="skip the gate_up SwiGLU and add_rms_norm_stats sweeps")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the C4 sharded, C5 ragged, read-roof and host-wall blocks")
-    ap.add_argument("--only", choices=["read_roof", "c4_kernels", "c2_kernels"],
+    ap.add_argument("--only", choices=["read_roof", "c4_kernels", "c2_kernels", "c4_step", "gateup_70b_shard"],
                     help="run one block alone on cuda:0 and print its JSON (entry points for profiling)")
+    ap.add_argument("--shard-ranks", type=int, default=8, choices=[1, 2, 4, 8],
+                    help="--only gateup_70b_shard: the per-rank column width of this many ranks")
     args = ap.parse_args()
     if args.only:
         print(json.dumps(run_only(args), default=_jsonable), flush=True)
