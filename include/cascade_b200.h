@@ -232,8 +232,11 @@ CASCADE_API int cascade_probe_hbm_read(const void *src, size_t bytes, int32_t mo
 /* Last error message of this thread ("" if none). */
 CASCADE_API const char *cascade_last_error(void);
 
-/* Reads and clears the device error word (non-zero = a kernel's bounded
- * wait gave up). Synchronises the current device. */
+/* Reads and clears the device error word. Bits: 1 = a kernel's bounded wait
+ * gave up; 2 = a block id outside the pool was read as a zero page; 4 = a
+ * stage-1 piece fell outside its planned partial planes and was skipped (its
+ * rows are garbage; the planner's bound rules this out). Synchronises the
+ * current device. */
 CASCADE_API int cascade_device_error(uint32_t *word);
 
 /* Library version (major*10000 + minor*100 + patch). */

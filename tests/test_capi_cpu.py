@@ -174,3 +174,85 @@ def test_planner_planned_decode_choice_and_workspace():
     assert plan(64, 8, bs=128, KVH=8).kernel == 0
     d = _desc(num_tokens=512, batch=512, kv_heads=8, num_heads=40, block_size=16, block_cols=290, q_seqlen_value=0)
     assert capi.plan(d, 1, True).kernel == 0  # per-request q lengths: never planned
+
+
+def _two_segment_pieces(T, tc, ga, gb, TA):
+    """Restatement of the stage-1 wrapper's run map (prefix_tc.cu): runs
+    [0, ga) cut [0, TA), runs [ga, ga + gb) cut [TA, T) (TA = T: one
+    segment); a piece is a run's part inside one unit of tc tiles, written to
+    plane run - run_of(unit's first tile). Returns {unit: [(start, end, plane)]}."""
+    def bnd(r):
+        return r * TA // ga if r <= ga else TA + (r - ga) * (T - TA) // gb
+
+    def run_of(x):
+        if x < TA:
+            return ((x + 1) * ga + TA - 1) // TA - 1
+        return ga + ((x - TA + 1) * gb + (T - TA) - 1) // (T - TA) - 1
+
+    out = {}
+    for run in range(ga + gb):
+        x, hi = bnd(run), bnd(run + 1)
+        while x < hi:
+            u = x // tc
+            end = min(hi, (u + 1) * tc)
+            out.setdefault(u, []).append((x - u * tc, end - u * tc, run - run_of(u * tc)))
+            x = end
+    return out
+
+
+def _overlap_tiles(tokens, kv_heads, ga, T):
+    """Restatement of overlap_tiles (kernels.h): segment A's tiles from the
+    suffix's kv tokens (6 TB/s decode, 3.3 us per stage-1 tile, runs of 32
+    tiles or none, at most 3/5 of the tiles)."""
+    per_run = int(tokens * kv_heads * 512.0 / 6000.0 / 3300.0)
+    per_run = min(per_run, (3 * T) // 5 // ga)
+    return 0 if per_run < 32 else per_run * ga
+
+
+@pytest.mark.parametrize("kv_heads", [8, 4, 2])
+def test_overlapped_stage1_schedule_and_workspace(kv_heads):
+    """The C4 step (4 groups x 64 requests, prefix 16384, suffix <= 2048 on the
+    per-item decode) runs stage-1 in two segments around the decode: 24 runs
+    (48 CTAs) over the first TA tiles, the 74-run equal schedule over the rest.
+    For every TA the device can choose, each unit's pieces cover its tiles
+    once, in order, on planes 0, 1, ... below the planner's bound, which the
+    step's workspace size holds. kv_heads 4: the shard of 2 ranks (13 planes);
+    kv_heads 2 (4 ranks): too few tiles, the serial order."""
+    from cascade_kernel import capi
+    pre = _desc(num_tokens=256, num_heads=8 * kv_heads, kv_heads=kv_heads, batch=4, block_cols=128,
+                q_seqlen_value=64, num_blocks=40000)
+    suf = _desc(num_tokens=256, num_heads=8 * kv_heads, kv_heads=kv_heads, batch=256, block_cols=16,
+                q_seqlen_value=1, num_blocks=40000)
+    pa, pb = capi.plan(pre, 64, True), capi.plan(suf, 1, True)
+    assert pa.kernel == 1 and pb.kernel == 0 and pb.num_splits == (2 if kv_heads == 8 else 4)
+    tc, ga, gb = 128, 24, 74
+    T = kv_heads * 4 * tc
+    minrun = min(32, (T - 3 * T // 5) // gb)
+    got = capi.decode_step_workspace_size(pre, suf)
+    align = lambda n: -(-n // 256) * 256
+    if minrun < 8:
+        # segment B's runs would be shorter than 8 tiles (the 4-rank shard):
+        # no overlap, the plan's own planes
+        assert got == align(pa.workspace_bytes) + align(pb.workspace_bytes)
+        return
+    bound = -(-tc // minrun) + 1
+    rows = 256 * 8 * kv_heads
+    assert got == align(bound * rows * 129 * 4) + align(pb.workspace_bytes)
+    TAs = [0] + [r * ga for r in range(32, (3 * T) // 5 // ga + 1)]
+    for TA in TAs:
+        for u, ps in _two_segment_pieces(T, tc, ga, gb, TA).items():
+            assert [p[2] for p in ps] == list(range(len(ps))), (TA, u)
+            assert ps[0][0] == 0 and ps[-1][1] == tc and all(a[1] == b[0] for a, b in zip(ps, ps[1:]))
+            assert len(ps) <= bound
+    # a C4-sized suffix (256 requests, mean 1,152 tokens) sizes segment A at 61 tiles per run, ~36% of the tiles
+    assert _overlap_tiles(294912, 8, ga, 4096) == 61 * ga
+
+
+def test_overlap_not_used_for_small_or_planned_steps():
+    """C2 (prefix-first) keeps its workspace: no extra stage-1 planes."""
+    from cascade_kernel import capi
+    pre = _desc(num_tokens=64, batch=1, block_cols=32, q_seqlen_value=64)
+    suf = _desc(num_tokens=64, batch=64, block_cols=8, q_seqlen_value=1)
+    align = lambda n: -(-n // 256) * 256
+    assert capi.decode_step_workspace_size(pre, suf) == (align(capi.plan(pre, 64, True).workspace_bytes)
+                                                        + align(capi.plan(suf, 1, True).workspace_bytes))

@@ -6,8 +6,9 @@ heads) and the ragged stress case (C5: 32 groups, lognormal prefixes up to
 32768 tokens, block size 16, fp16, GQA 5, zero-length suffixes).
 
 Checks: the fused single-combine step and the reference consumer's three-op
-chain agree to within the chain's extra rounding (plus, on C2, the P-rounding
-structure of the fused step's prefix-first stage-1 splits) and are finite; the CPU
+chain agree to within the chain's extra rounding (plus, on C2 and C4, the
+P-rounding structure of the fused step's own stage-1 pieces: prefix-first
+splits, or two segments around the suffix decode) and are finite; the CPU
 oracle of the whole step, run on EVERY kv head (one spawned worker per kv
 head), matches the fused step at the BASELINE tolerance (2e-2) and at one
 output ulp plus the P-rounding structure slack."""
@@ -39,8 +40,10 @@ def test_full_size_step(name):
     assert np.isfinite(a).all() and np.isfinite(b).all()
     # the chain rounds the suffix partial once more; on C2 the fused step also
     # runs stage-1 with its prefix-first splits (fewer, longer than the
-    # standalone op's), which moves where P is rounded: the structure slack
-    slack = 2e-3 if name == "c2" else 1e-7
+    # standalone op's), and on C4 with its two segments around the suffix
+    # decode (other piece boundaries), which moves where P is rounded: the
+    # structure slack
+    slack = 2e-3 if name in ("c2", "c4") else 1e-7
     bound = O.ulp(np.maximum(np.abs(a), np.abs(b)), dt) + 0.5 * O.ulp(Hh.dev_to_f64(o2), dt) + slack
     assert (np.abs(a - b) <= bound).all(), float((np.abs(a - b) - bound).max())
 

@@ -112,6 +112,32 @@ bool pp_pieces(const cascade_paged_attn_t* p, int64_t* ctas, int64_t* unit_tiles
   return true;
 }
 
+// Stage-1 overlapped with the suffix decode in a decode-first cascade step
+// (PagedAttnLaunch::ov_seg): stage-1 on the equal-run schedule, the decode on
+// its per-item grid (the persistent planned decode keeps the serial order:
+// held SMs stall its fixed grid, C5 decode 206 -> 351 us with 24 SMs held).
+// Segment A = kOvCtas / pairs runs over the first TA tiles (TA decided on the
+// device, 0 or at least kOvMinRunTiles per run and at most 3/5 of the
+// tiles), segment B = the equal-run schedule's G runs over the rest. Every
+// run is then at least `minrun` tiles long, so a unit of tc tiles meets at
+// most ceil(tc / minrun) + 1 runs: *planes bounds its partial planes.
+bool overlap_plan(const cascade_paged_attn_t* a, int kernel_a, int kernel_b, int64_t n2, int64_t* runs_a,
+                  int64_t* runs_b, int64_t* planes) {
+  int64_t ctas, tc, pl;
+  if (kernel_a != 1 || kernel_b != 0 || n2 <= 0 || !pp_pieces(a, &ctas, &tc, &pl)) return false;
+  const int64_t pairs = ceil_div(a->q_seqlen_value * (a->num_heads / a->kv_heads), 256);
+  const int64_t ga = std::max<int64_t>(1, kOvCtas / pairs), gb = ctas / pairs;
+  const int64_t T = a->kv_heads * a->batch * tc;
+  const int64_t minrun = std::min<int64_t>(kOvMinRunTiles, (T - (3 * T) / 5) / gb);
+  if (minrun < kMinRunTiles) return false;
+  const int64_t np = ceil_div(tc, minrun) + 1;
+  if (np > kMaxSplits || np + n2 > 64) return false;
+  *runs_a = ga;
+  *runs_b = gb;
+  *planes = np;
+  return true;
+}
+
 // Shape-only split rule of each kernel.
 void split_rule(const cascade_paged_attn_t* p, int kernel, int64_t* split_tokens, int64_t* num_splits) {
   const int64_t cap = std::max<int64_t>(1, p->block_cols * p->block_size);
@@ -528,7 +554,15 @@ size_t cascade_decode_step_workspace_size(const cascade_paged_attn_t* prefix, co
   cascade_paged_attn_t a = *prefix, b = *suffix;
   a.flags |= CASCADE_FLAG_PARTIALS_ONLY;
   b.flags |= CASCADE_FLAG_PARTIALS_ONLY;
-  return align_up(workspace_size_any(&a, 1), 256) + align_up(workspace_size_any(&b, 1), 256);
+  size_t need_a = workspace_size_any(&a, 1);
+  cascade_attn_plan_t pa, pb;
+  int64_t ra, rb, planes;
+  if (a.q_seqlen_value > 0 && b.q_seqlen_value > 0 && a.batch > 0 && b.batch > 0 && a.num_tokens > 0 &&
+      cascade_plan_paged_attn(&a, a.q_seqlen_value, 1, &pa) == CASCADE_OK &&
+      cascade_plan_paged_attn(&b, b.q_seqlen_value, 1, &pb) == CASCADE_OK &&
+      overlap_plan(&a, pa.kernel, pb.kernel, pb.num_splits, &ra, &rb, &planes))
+    need_a = std::max(need_a, workspace_for(&a, planes, 1));
+  return align_up(need_a, 256) + align_up(workspace_size_any(&b, 1), 256);
 }
 
 int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_attn_t* suffix, void* out,
@@ -553,12 +587,6 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
   int rc = prepare_paged(&a, op, true, st, &pa, &La);
   if (rc == CASCADE_OK) rc = prepare_paged(&b, op, true, st, &pb, &Lb);
   if (rc) return rc;
-  const size_t need_a = pa.num_splits ? align_up(pa.workspace_bytes, 256) : 0;
-  const size_t need_b = pb.num_splits ? align_up(pb.workspace_bytes, 256) : 0;
-  rc = check_workspace(op, workspace, workspace_bytes, need_a + need_b);
-  if (rc) return rc;
-  set_partials(&La, workspace, pa.kernel);
-  set_partials(&Lb, static_cast<uint8_t*>(workspace) + need_a, pb.kernel);
   const bool fp16 = suffix->dtype == CASCADE_FP16;
   // Prefix-first schedule (a small stage-1 grid, e.g. the Llama-3-8B step):
   // stage-1 runs first on about kPrefixFirstCtas SMs with fewer, longer
@@ -568,13 +596,37 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
   int64_t pf_splits = 0;
   const bool prefix_first = pa.num_splits && pa.kernel == 1 && pb.num_splits &&
                             prefix_first_splits(&a, &pf_splits);
+  // Overlap (decode-first steps with a long stage-1): stage-1 segment A first
+  // on kOvCtas SMs, the decode as its programmatic dependent on the others
+  // (only its last CTA waits for segment A), segment B after the decode on
+  // all SMs (each CTA waits for the decode before exiting), so the
+  // tensor-bound stage-1 runs beside the HBM-bound decode instead of after it.
+  // Its stage-1 partial planes are sized by overlap_plan's bound (the same
+  // rule cascade_decode_step_workspace_size applies).
+  int64_t ov_a = 0, ov_b = 0, ov_planes = 0;
+  const bool overlap = !prefix_first && pa.num_splits && pb.num_splits && a.q_seqlen_value > 0 &&
+                       b.q_seqlen_value > 0 &&
+                       overlap_plan(&a, pa.kernel, pb.kernel, Lb.num_splits, &ov_a, &ov_b, &ov_planes);
+  size_t need_a = pa.num_splits ? align_up(pa.workspace_bytes, 256) : 0;
+  if (overlap) need_a = std::max(need_a, align_up(workspace_for(&a, ov_planes, pa.kernel), 256));
+  const size_t need_b = pb.num_splits ? align_up(pb.workspace_bytes, 256) : 0;
+  rc = check_workspace(op, workspace, workspace_bytes, need_a + need_b);
+  if (rc) return rc;
   if (prefix_first) {
     const int64_t cap = std::max<int64_t>(1, a.block_cols * a.block_size);
     La.split_tokens = static_cast<int32_t>(ceil_div(ceil_div(cap, pf_splits), kTcTile) * kTcTile);
     La.num_splits = static_cast<int32_t>(ceil_div(cap, La.split_tokens));
     La.piece_ctas = 0;  // the split grid
-    set_partials(&La, workspace, pa.kernel);
   }
+  if (overlap) {
+    La.num_splits = static_cast<int32_t>(ov_planes);
+    La.ov_runs_a = static_cast<int32_t>(ov_a);
+    La.ov_runs_b = static_cast<int32_t>(ov_b);
+    La.ov_lens = b.actual_kv_seqlens;
+    La.ov_nlens = static_cast<int32_t>(b.batch);
+  }
+  set_partials(&La, workspace, pa.kernel);
+  set_partials(&Lb, static_cast<uint8_t*>(workspace) + need_a, pb.kernel);
   if ((pa.num_splits ? La.num_splits : 0) + (pb.num_splits ? Lb.num_splits : 0) > 64)
     return fail(CASCADE_ERR_UNSUPPORTED, "%s: more than 64 KV splits per row", op);
   cudaError_t e = cudaSuccess;
@@ -587,6 +639,19 @@ int cascade_decode_step(const cascade_paged_attn_t* prefix, const cascade_paged_
     e = launch_attention(La, pa.kernel, fp16, st);
     Lb.pdl = 2;  // only its last CTA waits for stage-1: no slot is held while stage-1 runs
     if (e == cudaSuccess) e = launch_attention(Lb, pb.kernel, fp16, st);
+  } else if (overlap) {
+    const int64_t pairs = ceil_div(a.q_seqlen_value * (a.num_heads / a.kv_heads), 256);
+    PagedAttnLaunch LA = La, LB = La;
+    LA.ov_seg = 1;
+    LA.piece_ctas = static_cast<int32_t>(ov_a * pairs);
+    LA.pdl = 0;
+    LB.ov_seg = 2;
+    LB.piece_ctas = static_cast<int32_t>(ov_b * pairs);
+    LB.pdl = 1;
+    Lb.pdl = 2;
+    e = launch_attention(LA, pa.kernel, fp16, st);
+    if (e == cudaSuccess) e = launch_attention(Lb, pb.kernel, fp16, st);
+    if (e == cudaSuccess) e = launch_attention(LB, pa.kernel, fp16, st);
   } else {
     if (pb.num_splits) e = launch_attention(Lb, pb.kernel, fp16, st);
     La.pdl = pb.num_splits ? 1 : 0;

@@ -10,6 +10,29 @@ namespace cascade {
 constexpr int kHeadDim = 128;
 constexpr int kNumSMs = 148;
 
+// Stage-1 overlapped with a cascade step's suffix decode (PagedAttnLaunch::
+// ov_seg): segment A runs on kOvCtas SMs beside the decode, sized so that its
+// runs last about as long as the decode: the suffix's kv bytes at
+// kOvDecodeBytesPerNs (the decode's HBM rate on the SMs segment A leaves it:
+// the C4 decode took 221 instead of 206 us with 48 SMs held) over kOvTileNs
+// per 128-token KV tile of a two-tile stage-1 CTA (C4: 55 tiles in ~175 us).
+// The estimate errs short: an early end of segment A idles its SMs until
+// segment B starts, a late one delays a third of segment B's CTAs. No segment
+// A below kOvMinRunTiles tiles per run; at most 3/5 of the tiles.
+constexpr int kOvCtas = 48;
+constexpr int64_t kOvMinRunTiles = 32;
+constexpr double kOvDecodeBytesPerNs = 6000.0;  // 6 TB/s
+constexpr double kOvTileNs = 3300.0;
+__host__ __device__ inline int64_t overlap_tiles(int64_t suffix_tokens, int64_t kv_heads, int64_t runs_a,
+                                                 int64_t T) {
+  const double t_dec = static_cast<double>(suffix_tokens) * static_cast<double>(kv_heads) * 512.0 /
+                       kOvDecodeBytesPerNs;
+  int64_t per_run = static_cast<int64_t>(t_dec / kOvTileNs);
+  const int64_t cap = (3 * T) / 5 / runs_a;
+  if (per_run > cap) per_run = cap;
+  return per_run < kOvMinRunTiles ? 0 : per_run * runs_a;
+}
+
 // ----------------------------------------------------------------------------
 // paged attention (decode path: <= 16 query rows per (request, kv head))
 // ----------------------------------------------------------------------------
@@ -35,6 +58,14 @@ struct PagedAttnLaunch {
   // equal runs, each CTA taking one run (one or two pieces of units); a
   // piece's partial goes to plane "its index among the unit's pieces"
   int32_t piece_ctas, piece_unit_tiles;
+  // Equal runs in two segments around a cascade step's suffix decode
+  // (ov_seg 0: one segment of piece_ctas / pairs runs). The first TA tiles
+  // are cut into ov_runs_a runs (segment A, launched before the decode on few
+  // SMs: ov_seg 1), the rest into ov_runs_b runs (segment B, launched after
+  // it: ov_seg 2). Every CTA of both launches computes the same TA from the
+  // suffix's kv lengths (ov_lens, ov_nlens requests).
+  int32_t ov_seg, ov_runs_a, ov_runs_b, ov_nlens;
+  const int64_t* ov_lens;
   int32_t out_dtype;    // 0 bf16, 1 fp16, 2 fp32
   int32_t lse_stride;   // 8 (reference padded rows) or 1 (compact)
   int32_t partial_out;  // 1: always write split partials (a later combine produces the output)

@@ -620,6 +620,7 @@ struct __align__(8) PpBars {
   uint64_t o_final[2];
   uint64_t stall, drain;
   uint32_t tmem_base;
+  int64_t ov_ta;  // segment A's tile count of an overlapped stage-1 (ov_seg != 0)
 };
 static_assert(sizeof(PpBars) <= 256, "barrier block");
 constexpr int kPpNumBars = static_cast<int>(offsetof(PpBars, tmem_base) / sizeof(uint64_t));
@@ -1010,6 +1011,18 @@ __global__ void __launch_bounds__(kPpThreads, 1) paged_prefix_pp_kernel(const __
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
+  const int64_t mtiles = (static_cast<int64_t>(p.max_q_seqlen) * p.group + kRows - 1) / kRows;
+  const int64_t pairs = (mtiles + 1) / 2;
+  const int64_t T = static_cast<int64_t>(p.batch) * p.kv_heads * p.piece_unit_tiles;
+  if (p.ov_seg != 0 && threadIdx.x < 32) {
+    // overlapped with the suffix decode: segment A's share of the tiles from
+    // the suffix's kv tokens (the same sum, hence the same value, in every CTA)
+    long long tok = 0;
+    for (int b = threadIdx.x; b < p.ov_nlens; b += 32) tok += p.ov_lens[b];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tok += __shfl_xor_sync(0xffffffffu, tok, o);
+    if (threadIdx.x == 0) bars->ov_ta = overlap_tiles(tok, p.kv_heads, p.ov_runs_a, T);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1023,25 +1036,38 @@ __global__ void __launch_bounds__(kPpThreads, 1) paged_prefix_pp_kernel(const __
     // equal runs of the concatenated (request, kv head) KV streams' tiles, each
     // run taken by `pairs` adjacent CTAs (one per row-tile pair of the
     // stream), so the pairs that read the same K/V tiles run in lock step and
-    // share them through L2. A stream's pieces are numbered by the runs that
-    // hold them, starting at the run that holds its first tile: cf(x) = the
-    // run containing tile x, the largest r with floor(r T / G) <= x
-    const int64_t mtiles = (static_cast<int64_t>(p.max_q_seqlen) * p.group + kRows - 1) / kRows;
-    const int64_t pairs = (mtiles + 1) / 2;
+    // share them through L2. One segment: G runs over [0, T). Overlapped with
+    // the suffix decode: ga runs over [0, TA) (segment A) and gb runs over
+    // [TA, T) (segment B), run numbers continuing from A into B. A stream's
+    // pieces are numbered by the runs that hold them, starting at the run that
+    // holds its first tile: run_of(x) = the largest r with bnd(r) <= x.
     const int64_t tc = p.piece_unit_tiles;
-    const int64_t G = gridDim.x / pairs;
-    const int64_t T = static_cast<int64_t>(p.batch) * p.kv_heads * tc;
-    const int64_t run = blockIdx.x / pairs;
+    int64_t ga, gb, TA, run;
+    if (p.ov_seg == 0) {
+      ga = gridDim.x / pairs, gb = 0, TA = T;
+      run = blockIdx.x / pairs;
+    } else {
+      ga = p.ov_runs_a, gb = p.ov_runs_b, TA = bars->ov_ta;
+      run = (p.ov_seg == 2 ? ga : 0) + blockIdx.x / pairs;
+    }
+    auto bnd = [&](int64_t r) -> int64_t { return r <= ga ? r * TA / ga : TA + (r - ga) * (T - TA) / gb; };
+    auto run_of = [&](int64_t x) -> int64_t {
+      return x < TA ? ((x + 1) * ga + TA - 1) / TA - 1 : ga + ((x - TA + 1) * gb + (T - TA) - 1) / (T - TA) - 1;
+    };
     const int mp = static_cast<int>(blockIdx.x % pairs);
-    const int64_t hi = (run + 1) * T / G;
+    const int64_t hi = bnd(run + 1);
     bool live = false;
-    for (int64_t x = run * T / G; x < hi;) {
+    for (int64_t x = bnd(run); x < hi;) {
       const int64_t u = x / tc;
       const int64_t ue = (u + 1) * tc;
       const int64_t end = min(hi, ue);
-      const int64_t cf = ((u * tc + 1) * G + T - 1) / T - 1;
+      const int64_t plane = run - run_of(u * tc);
+      if (plane >= p.num_splits) {  // outside the planned planes (the planner's bound rules this out)
+        if (threadIdx.x == 0) atomicOr(&g_cascade_device_error, kErrBadPlan);
+        break;
+      }
       live = paged_prefix_pp_piece<kFp16>(p, smem, tbase, static_cast<int>(u / p.kv_heads),
-                                          static_cast<int>(u % p.kv_heads), mp, static_cast<int>(run - cf),
+                                          static_cast<int>(u % p.kv_heads), mp, static_cast<int>(plane),
                                           static_cast<int>((x - u * tc) * kTok), static_cast<int>((end - u * tc) * kTok),
                                           end == ue ? p.num_splits : 0, live);
       x = end;

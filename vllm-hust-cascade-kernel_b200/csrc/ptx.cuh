@@ -21,13 +21,15 @@
 
 namespace cascade {
 
-// Device error word (bit set = a bounded wait gave up somewhere, or a block
-// id outside the pool was met and replaced by a zero-filled page).
+// Device error word (bit set = a bounded wait gave up somewhere, a block
+// id outside the pool was met and replaced by a zero-filled page, or a
+// stage-1 piece fell outside its planned partial planes and was skipped).
 extern __device__ unsigned int g_cascade_device_error;
 
 enum : unsigned int {
   kErrMbarTimeout = 1u,
   kErrBadBlockId = 2u,
+  kErrBadPlan = 4u,
 };
 
 constexpr uint64_t kWaitLimitNs = 100ull * 1000 * 1000;   // one wait
