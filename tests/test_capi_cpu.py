@@ -200,20 +200,34 @@ def _two_segment_pieces(T, tc, ga, gb, TA):
     return out
 
 
-def _overlap_tiles(tokens, kv_heads, ga, T):
+def _overlap_tiles(tokens, kv_heads, ga, gb, T, tc):
     """Restatement of overlap_tiles (kernels.h): segment A's tiles from the
-    suffix's kv tokens (6 TB/s decode, 3.3 us per stage-1 tile, runs of 32
-    tiles or none, at most 3/5 of the tiles)."""
+    suffix's kv tokens (6 TB/s decode, 3.3 us per stage-1 tile, runs of at
+    least 32 tiles or none, at most 3/5 of the tiles); within 40% of that,
+    the size whose segment-B runs are tc >> k tiles."""
     per_run = int(tokens * kv_heads * 512.0 / 6000.0 / 3300.0)
     per_run = min(per_run, (3 * T) // 5 // ga)
-    return 0 if per_run < 32 else per_run * ga
+    if per_run < 32:
+        return 0
+    est = per_run * ga
+    best = None
+    for k in range(4):
+        lb = tc >> k
+        if lb < 8 or (lb << k) != tc:
+            break
+        ta = T - gb * lb
+        if ta < 32 * ga or ta > (3 * T) // 5 or 5 * abs(ta - est) > 2 * est:
+            continue
+        if best is None or abs(ta - est) < abs(best - est):
+            best = ta
+    return est if best is None else best
 
 
 @pytest.mark.parametrize("kv_heads", [8, 4, 2])
 def test_overlapped_stage1_schedule_and_workspace(kv_heads):
     """The C4 step (4 groups x 64 requests, prefix 16384, suffix <= 2048 on the
-    per-item decode) runs stage-1 in two segments around the decode: 24 runs
-    (48 CTAs) over the first TA tiles, the 74-run equal schedule over the rest.
+    per-item decode) runs stage-1 in two segments around the decode: 32 runs
+    (64 CTAs) over the first TA tiles, the 74-run equal schedule over the rest.
     For every TA the device can choose, each unit's pieces cover its tiles
     once, in order, on planes 0, 1, ... below the planner's bound, which the
     step's workspace size holds. kv_heads 4: the shard of 2 ranks (13 planes);
@@ -225,7 +239,7 @@ def test_overlapped_stage1_schedule_and_workspace(kv_heads):
                 q_seqlen_value=1, num_blocks=40000)
     pa, pb = capi.plan(pre, 64, True), capi.plan(suf, 1, True)
     assert pa.kernel == 1 and pb.kernel == 0 and pb.num_splits == (2 if kv_heads == 8 else 4)
-    tc, ga, gb = 128, 24, 74
+    tc, ga, gb = 128, 32, 74
     T = kv_heads * 4 * tc
     minrun = min(32, (T - 3 * T // 5) // gb)
     got = capi.decode_step_workspace_size(pre, suf)
@@ -238,14 +252,20 @@ def test_overlapped_stage1_schedule_and_workspace(kv_heads):
     bound = -(-tc // minrun) + 1
     rows = 256 * 8 * kv_heads
     assert got == align(bound * rows * 129 * 4) + align(pb.workspace_bytes)
-    TAs = [0] + [r * ga for r in range(32, (3 * T) // 5 // ga + 1)]
+    # every TA the device can choose: a multiple of ga with runs of >= 32 tiles
+    # up to 3/5 of the tiles, or T - gb * (tc >> k) in that range
+    TAs = [0] + sorted(set([r * ga for r in range(32, (3 * T) // 5 // ga + 1)]
+                           + [T - gb * (tc >> k) for k in range(4) if 32 * ga <= T - gb * (tc >> k) <= 3 * T // 5]))
     for TA in TAs:
         for u, ps in _two_segment_pieces(T, tc, ga, gb, TA).items():
             assert [p[2] for p in ps] == list(range(len(ps))), (TA, u)
             assert ps[0][0] == 0 and ps[-1][1] == tc and all(a[1] == b[0] for a, b in zip(ps, ps[1:]))
             assert len(ps) <= bound
-    # a C4-sized suffix (256 requests, mean 1,152 tokens) sizes segment A at 61 tiles per run, ~36% of the tiles
-    assert _overlap_tiles(294912, 8, ga, 4096) == 61 * ga
+    # the C4 suffix of bench.py's seed (304,653 tokens): 63 tiles per run
+    # estimated (2,016 tiles); 32-tile segment-B runs (TA = 4096 - 74 * 32 =
+    # 1,728) lie within 40% of it and are taken
+    if kv_heads == 8:
+        assert _overlap_tiles(304653, 8, ga, gb, T, tc) == 1728
 
 
 def test_overlap_not_used_for_small_or_planned_steps():

@@ -14,23 +14,37 @@ constexpr int kNumSMs = 148;
 // ov_seg): segment A runs on kOvCtas SMs beside the decode, sized so that its
 // runs last about as long as the decode: the suffix's kv bytes at
 // kOvDecodeBytesPerNs (the decode's HBM rate on the SMs segment A leaves it:
-// the C4 decode took 221 instead of 206 us with 48 SMs held) over kOvTileNs
-// per 128-token KV tile of a two-tile stage-1 CTA (C4: 55 tiles in ~175 us).
-// The estimate errs short: an early end of segment A idles its SMs until
-// segment B starts, a late one delays a third of segment B's CTAs. No segment
-// A below kOvMinRunTiles tiles per run; at most 3/5 of the tiles.
-constexpr int kOvCtas = 48;
+// the C4 decode took 221 instead of 206 us with 48 SMs held, 254 with 64)
+// over kOvTileNs per 128-token KV tile of a two-tile stage-1 CTA (C4: 55
+// tiles in ~175 us). Within 40% of that estimate, the segment A whose
+// segment-B runs are a whole fraction of a stream (tc >> k tiles, TA = T -
+// runs_b * (tc >> k)) is taken instead: no segment-B run then straddles two
+// (request, kv head) streams and every segment-B CTA does one piece (C4:
+// 343 us at TA = 1,728 tiles, 32-tile runs, against 345-361 us for segments
+// whose runs straddle streams). No segment A below kOvMinRunTiles tiles per
+// run; at most 3/5 of the tiles.
+constexpr int kOvCtas = 64;
 constexpr int64_t kOvMinRunTiles = 32;
 constexpr double kOvDecodeBytesPerNs = 6000.0;  // 6 TB/s
 constexpr double kOvTileNs = 3300.0;
 __host__ __device__ inline int64_t overlap_tiles(int64_t suffix_tokens, int64_t kv_heads, int64_t runs_a,
-                                                 int64_t T) {
+                                                 int64_t runs_b, int64_t T, int64_t tc) {
   const double t_dec = static_cast<double>(suffix_tokens) * static_cast<double>(kv_heads) * 512.0 /
                        kOvDecodeBytesPerNs;
   int64_t per_run = static_cast<int64_t>(t_dec / kOvTileNs);
   const int64_t cap = (3 * T) / 5 / runs_a;
   if (per_run > cap) per_run = cap;
-  return per_run < kOvMinRunTiles ? 0 : per_run * runs_a;
+  if (per_run < kOvMinRunTiles) return 0;
+  const int64_t est = per_run * runs_a;
+  int64_t best = -1;
+  for (int k = 0; k < 4; ++k) {
+    const int64_t lb = tc >> k;
+    if (lb < 8 || (lb << k) != tc) break;
+    const int64_t ta = T - runs_b * lb;
+    if (ta < kOvMinRunTiles * runs_a || ta > (3 * T) / 5 || 5 * (ta > est ? ta - est : est - ta) > 2 * est) continue;
+    if (best < 0 || (ta > est ? ta - est : est - ta) < (best > est ? best - est : est - best)) best = ta;
+  }
+  return best >= 0 ? best : est;
 }
 
 // ----------------------------------------------------------------------------

@@ -1021,7 +1021,7 @@ __global__ void __launch_bounds__(kPpThreads, 1) paged_prefix_pp_kernel(const __
     for (int b = threadIdx.x; b < p.ov_nlens; b += 32) tok += p.ov_lens[b];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) tok += __shfl_xor_sync(0xffffffffu, tok, o);
-    if (threadIdx.x == 0) bars->ov_ta = overlap_tiles(tok, p.kv_heads, p.ov_runs_a, T);
+    if (threadIdx.x == 0) bars->ov_ta = overlap_tiles(tok, p.kv_heads, p.ov_runs_a, p.ov_runs_b, T, p.piece_unit_tiles);
   }
   tc_fence_before();
   __syncthreads();
