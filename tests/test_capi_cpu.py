@@ -203,11 +203,11 @@ def _two_segment_pieces(T, tc, ga, gb, TA):
 def _overlap_tiles(tokens, kv_heads, ga, gb, T, tc):
     """Restatement of overlap_tiles (kernels.h): segment A's tiles from the
     suffix's kv tokens (6 TB/s decode, 3.3 us per stage-1 tile, runs of at
-    least 32 tiles or none, at most 3/5 of the tiles); within 40% of that,
+    least 16 tiles or none, at most 3/5 of the tiles); within 40% of that,
     the size whose segment-B runs are tc >> k tiles."""
     per_run = int(tokens * kv_heads * 512.0 / 6000.0 / 3300.0)
     per_run = min(per_run, (3 * T) // 5 // ga)
-    if per_run < 32:
+    if per_run < 16:
         return 0
     est = per_run * ga
     best = None
@@ -216,7 +216,7 @@ def _overlap_tiles(tokens, kv_heads, ga, gb, T, tc):
         if lb < 8 or (lb << k) != tc:
             break
         ta = T - gb * lb
-        if ta < 32 * ga or ta > (3 * T) // 5 or 5 * abs(ta - est) > 2 * est:
+        if ta < 16 * ga or ta > (3 * T) // 5 or 5 * abs(ta - est) > 2 * est:
             continue
         if best is None or abs(ta - est) < abs(best - est):
             best = ta
@@ -230,8 +230,8 @@ def test_overlapped_stage1_schedule_and_workspace(kv_heads):
     (64 CTAs) over the first TA tiles, the 74-run equal schedule over the rest.
     For every TA the device can choose, each unit's pieces cover its tiles
     once, in order, on planes 0, 1, ... below the planner's bound, which the
-    step's workspace size holds. kv_heads 4: the shard of 2 ranks (13 planes);
-    kv_heads 2 (4 ranks): too few tiles, the serial order."""
+    step's workspace size holds (9 planes on C4). kv_heads 4: the shard of 2
+    ranks (13 planes); kv_heads 2 (4 ranks): too few tiles, the serial order."""
     from cascade_kernel import capi
     pre = _desc(num_tokens=256, num_heads=8 * kv_heads, kv_heads=kv_heads, batch=4, block_cols=128,
                 q_seqlen_value=64, num_blocks=40000)
@@ -241,7 +241,7 @@ def test_overlapped_stage1_schedule_and_workspace(kv_heads):
     assert pa.kernel == 1 and pb.kernel == 0 and pb.num_splits == (2 if kv_heads == 8 else 4)
     tc, ga, gb = 128, 32, 74
     T = kv_heads * 4 * tc
-    minrun = min(32, (T - 3 * T // 5) // gb)
+    minrun = min(16, (T - 3 * T // 5) // gb)
     got = capi.decode_step_workspace_size(pre, suf)
     align = lambda n: -(-n // 256) * 256
     if minrun < 8:
@@ -252,10 +252,10 @@ def test_overlapped_stage1_schedule_and_workspace(kv_heads):
     bound = -(-tc // minrun) + 1
     rows = 256 * 8 * kv_heads
     assert got == align(bound * rows * 129 * 4) + align(pb.workspace_bytes)
-    # every TA the device can choose: a multiple of ga with runs of >= 32 tiles
+    # every TA the device can choose: a multiple of ga with runs of >= 16 tiles
     # up to 3/5 of the tiles, or T - gb * (tc >> k) in that range
-    TAs = [0] + sorted(set([r * ga for r in range(32, (3 * T) // 5 // ga + 1)]
-                           + [T - gb * (tc >> k) for k in range(4) if 32 * ga <= T - gb * (tc >> k) <= 3 * T // 5]))
+    TAs = [0] + sorted(set([r * ga for r in range(16, (3 * T) // 5 // ga + 1)]
+                           + [T - gb * (tc >> k) for k in range(4) if 16 * ga <= T - gb * (tc >> k) <= 3 * T // 5]))
     for TA in TAs:
         for u, ps in _two_segment_pieces(T, tc, ga, gb, TA).items():
             assert [p[2] for p in ps] == list(range(len(ps))), (TA, u)
@@ -266,6 +266,8 @@ def test_overlapped_stage1_schedule_and_workspace(kv_heads):
     # 1,728) lie within 40% of it and are taken
     if kv_heads == 8:
         assert _overlap_tiles(304653, 8, ga, gb, T, tc) == 1728
+    if kv_heads == 4:  # 31 tiles per run estimated (992); 16-tile segment-B runs: 2048 - 74 * 16 = 864
+        assert _overlap_tiles(304653, 4, ga, gb, T, tc) == 864
 
 
 def test_overlap_not_used_for_small_or_planned_steps():

@@ -22,9 +22,11 @@ constexpr int kNumSMs = 148;
 // (request, kv head) streams and every segment-B CTA does one piece (C4:
 // 343 us at TA = 1,728 tiles, 32-tile runs, against 345-361 us for segments
 // whose runs straddle streams). No segment A below kOvMinRunTiles tiles per
-// run; at most 3/5 of the tiles.
+// run (16: the 2-rank shard of C4, 4 kv heads, gets a segment A of 864 tiles,
+// 203 instead of 206 us serial; with 32 it had none); at most 3/5 of the
+// tiles.
 constexpr int kOvCtas = 64;
-constexpr int64_t kOvMinRunTiles = 32;
+constexpr int64_t kOvMinRunTiles = 16;
 constexpr double kOvDecodeBytesPerNs = 6000.0;  // 6 TB/s
 constexpr double kOvTileNs = 3300.0;
 __host__ __device__ inline int64_t overlap_tiles(int64_t suffix_tokens, int64_t kv_heads, int64_t runs_a,
