@@ -325,3 +325,42 @@ def test_layers_graph_overlapped_host_io_reuses_buffers_safely(use, io_group):
         torch.cuda.synchronize()
         for i in range(len(use)):
             assert torch.equal(io[i][2], cascade_decode(qs[i], pools[i][0], pools[i][1], t).cpu())
+
+
+@pytest.mark.parametrize("suffix", ["long", "empty"])
+def test_overlapped_stage1_other_shapes_vs_oracle(suffix):
+    """The step's two-segment stage-1 away from the C4 shape: one group of 64
+    requests, 64 q / 8 kv heads, a 24,576-token prefix (8 streams of 192
+    tiles: the overlap is planned with 25 partial planes). Suffixes U[1000,
+    2000] (98,819 tokens) give a segment A of 640 tiles (20 per run, no
+    stream-aligned size within reach); near-empty suffixes (zeros and a few
+    1-3 token ones) give none, the decode and segment B then doing all the
+    work. Checked against
+    the CPU oracle on every kv head."""
+    import torch
+    from cascade_kernel import capi
+    from cascade_kernel.cascade import cascade_decode
+    Hh.need_cuda()
+    rng = np.random.default_rng(21)
+    lens = (list(rng.integers(1000, 2001, 64)) if suffix == "long"
+            else [0] * 60 + [1, 2, 3, 1])
+    w = _work("ovl_" + suffix, group_sizes=[64], prefix_lens=[24576], suffix_lens=lens, H=64, KVH=8, bs=128,
+              dtype=torch.bfloat16, seed=22)
+    t = w.tables
+    dp = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.prefix_block_table, t.prefix_q_seqlens, t.prefix_kv_seqlens,
+                         t.uniform_group)
+    # the step writes split partials on both sides (the partials-only flag)
+    ds = capi.paged_desc(w.q, w.k_pool, w.v_pool, t.suffix_block_table, t.suffix_q_seqlens, t.suffix_kv_seqlens, 1,
+                         flags=capi.FLAG_PARTIALS_ONLY)
+    pb = capi.plan(ds, 1, True)
+    align = lambda n: -(-n // 256) * 256
+    # the step's workspace holds the overlap's 25 stage-1 planes
+    assert capi.decode_step_workspace_size(dp, ds) == align(25 * 64 * 64 * 129 * 4) + align(pb.workspace_bytes)
+    got = cascade_decode(w.q, w.k_pool, w.v_pool, t, fused=True)
+    torch.cuda.synchronize()
+    assert Hh.capi().device_error() == 0
+    a = Hh.dev_to_f64(got)
+    assert np.isfinite(a).all()
+    ref, _ = Hh.step_oracle_all_heads(w, out_dtype="fp32", round_suffix=False)
+    err = np.abs(a - ref)
+    assert (err <= O.ulp(ref, "bf16") + 2e-3).all(), float((err - O.ulp(ref, "bf16")).max())
