@@ -146,7 +146,11 @@ CASCADE_API int cascade_suffix_decode(const cascade_paged_attn_t *p, void *out, 
  * without the intermediate outputs; the suffix partial is not rounded to the
  * query dtype before the merge. `prefix` and `suffix` describe the same
  * query tensor (same num_tokens / num_heads / dtype); zero-length prefixes or
- * suffixes are allowed. */
+ * suffixes are allowed. The workspace size depends on the shapes alone; when a
+ * long stage-1 runs beside the suffix decode (stage-1 split into two launches
+ * around it) it covers that schedule's extra partial planes, so it can exceed
+ * the two standalone workspace sizes summed: size it with
+ * cascade_decode_step_workspace_size. */
 CASCADE_API size_t cascade_decode_step_workspace_size(const cascade_paged_attn_t *prefix,
                                                       const cascade_paged_attn_t *suffix);
 CASCADE_API int cascade_decode_step(const cascade_paged_attn_t *prefix, const cascade_paged_attn_t *suffix, void *out,
